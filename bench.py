@@ -1,0 +1,385 @@
+"""Benchmark of the paged decode attention hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+Default workload: Llama-3-8B-shape fp16 paged decode (H32/Hkv8/D128, batch
+64, context 2048, block size 16, shuffled 8192-block pool).  A step is one
+cottus_paged_decode call over the batch with every input already in HBM.
+Multi-GPU (torchrun, one process per GPU): each rank decodes its own batch
+of sequences (weak scaling, no collective); the long-context config instead
+splits every sequence's pages across the ranks and merges LSE partials over
+NCCL (strong scaling).  `--impl reference` times the reference's own CPU
+pagedAttentionCPU (compiled from its sources into oracle/_ref) on the host
+cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+sys.path.insert(0, str(ROOT / "cottus-runtime_b200"))
+
+METRIC = "paged-attn decode KV-read GB/s"
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def describe(w):
+    return (f"{w.name}: H{w.H}/Hkv{w.Hkv}/D{w.D}, batch {w.B}, context "
+            f"{int(w.ctx.min())}-{int(w.ctx.max())} (sum {int(w.ctx.sum())}), block 16, {w.num_blocks}-block pool")
+
+
+# -- clocks sampled during the timed region ---------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu, self.rows, self.proc = gpu_index, [], None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        rows = [r for r in self.rows if len(r) >= 9]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for n, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+                "samples": len(rows), "reasons": sorted(reasons)}
+
+
+# -- CPU baseline (reference pagedAttentionCPU compiled from its sources) --------------------
+
+def cpu_reference_rate(w, t, target_s=8.0, max_seqs=None):
+    """Times the reference's CPU path on the host cores over a sample of the
+    workload's sequences; returns (GB/s, threads, sample description)."""
+    from oracle.oracle import Reference
+    from cottus_b200.workloads import host_subpool
+
+    ref = Reference()
+    threads = os.cpu_count() or 1
+    seqs = list(range(w.B if max_seqs is None else min(w.B, max_seqs)))
+    sub, bt, ctx = host_subpool(w, t["kv_pool"], seqs)
+    q = t["query"][seqs].float().cpu().numpy()
+    per = w.block_elems()
+    # rebase every sequence onto its own lowest block so int32 offsets stay in range
+    bases, bt2 = [], bt.copy()
+    for i in range(len(seqs)):
+        n = (int(ctx[i]) + w.bs - 1) // w.bs
+        lo = int(bt[i, :n].min()) if n else 0
+        bases.append(sub.ctypes.data + 2 * lo * per)
+        bt2[i, :n] -= lo
+    out = np.zeros((len(seqs), w.H * w.D), np.float32)
+    kvb = int(np.sum(ctx.astype(np.int64))) * 2 * w.Hkv * w.D * 2
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        ref.paged_attention_batch_rebased(out, q, bases, bt2, ctx, w.layer, w.H, w.Hkv, w.D, w.bs, w.L, threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= target_s or reps >= 1000:
+            break
+    return kvb * reps / el / 1e9, threads, f"{len(seqs)} of {w.B} sequences x {reps} passes ({el:.1f} s wall)"
+
+
+# -- main --------------------------------------------------------------------------------------
+
+def build_workload(name, rank):
+    from cottus_b200 import workloads as W
+
+    seed = 1000 + rank
+    return W.BUILDERS[name](seed=seed)
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU path, rank 0 only."""
+    import torch
+    if world > 1 and rank != 0:
+        return
+    from cottus_b200 import workloads as W
+    w = build_workload(args.config, 0)
+    t = W.device_tensors(w, "cpu" if not torch.cuda.is_available() else "cuda")
+    # bounded per-step sample: whole batch when it is cheap, else a prefix of sequences
+    max_seqs = 64 if w.name != "long_ctx_70b" else 1
+    rates = []
+    for _ in range(args.warmup):
+        cpu_reference_rate(w, t, target_s=0.0, max_seqs=max_seqs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        r, threads, sample = cpu_reference_rate(w, t, target_s=0.0, max_seqs=max_seqs)
+        rates.append(r)
+    el = time.perf_counter() - t0
+    v = float(np.mean(rates))
+    line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": el / max(args.steps, 1) * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": describe(w), "kv": "fp16"}, "impl": "reference",
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="llama3_8b",
+                    choices=["tinyllama_f32", "llama3_8b", "ragged_mha", "long_ctx_70b", "fused_tinyllama"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import cottus_b200 as cb
+    from cottus_b200 import workloads as W
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    split = args.config == "long_ctx_70b" and world > 1
+    w = build_workload(args.config, 0 if split else rank)
+    if split:
+        s = W.shard_long_context(w, rank, world)
+        t = W.device_tensors(s, dev, pool_blocks=s.meta["pool_range"])
+        t["block_table"] = torch.from_numpy(s.block_table).to(dev)
+        t["context_lens"] = torch.from_numpy(s.ctx).to(dev)
+        wl = s
+    else:
+        t = W.device_tensors(w, dev)
+        wl = w
+    if w.fused:
+        t["cos_sin"] = cb.rope_cos_sin_table(int(w.positions.max()) + 1, w.D, w.theta).to(dev)
+
+    stream = torch.cuda.current_stream(dev)
+    out = torch.empty((w.B, w.H, w.D), dtype=w.out_dtype, device=dev)
+    part = torch.empty((w.B, w.H, w.D), dtype=torch.float32, device=dev)
+    lse = torch.empty((w.B, w.H), dtype=torch.float32, device=dev)
+    pool_snapshot = t["kv_pool"].clone() if w.fused else None  # the fused step appends; restore is not timed
+
+    launches_per_step = 2
+
+    def step():
+        if w.fused:
+            cb.rope_append_decode(t["query"], t["key"], t["value"], t["positions"], t["cos_sin"], t["kv_pool"],
+                                  t["block_table"], num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs, out=out)
+        elif split:
+            from cottus_b200 import parallel
+            parallel.split_kv_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"],
+                                     num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
+                                     num_physical_blocks=wl.num_blocks, out_dtype=w.out_dtype, part=part, lse=lse)
+        else:
+            cb.paged_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], num_kv_heads=w.Hkv,
+                            head_dim=w.D, block_size=w.bs, out=out, num_physical_blocks=wl.num_blocks)
+
+    kv_bytes_rank = wl.kv_bytes()
+    small = w.kv_bytes() < 2 * L2_BYTES
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if small else None
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    if small:
+        # L2-resident working set: flush L2 between steps, time every step alone
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            evs[i][0].record(stream)
+            step()
+            evs[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        elapsed_ms = sum(a.elapsed_time(b) for a, b in evs)
+    else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        elapsed_ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    if world > 1:
+        tt = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(tt.item())
+    ms = elapsed_ms / args.steps
+
+    # the dominant kernel alone (decode kernel + its in-stream merge), one launch pair per event pair
+    ka = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(50)]
+    for a, b in ka:
+        if small:
+            flush.fill_(1.0)
+        a.record(stream)
+        if w.fused:
+            step()
+        else:
+            cb.paged_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], num_kv_heads=w.Hkv,
+                            head_dim=w.D, block_size=w.bs, out=part if split else out, lse_out=lse if split else None,
+                            num_physical_blocks=wl.num_blocks)
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    k_ms = float(np.mean([a.elapsed_time(b) for a, b in ka]))
+
+    # end to end through the C ABI with host buffers: H2D of q/table/lengths, D2H of the output
+    e2e = None
+    if not args.no_e2e and not split and not w.fused:
+        hq = t["query"].cpu().pin_memory()
+        hbt = t["block_table"].cpu().pin_memory()
+        hctx = t["context_lens"].cpu().pin_memory()
+        hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+        dq, dbt, dctx = torch.empty_like(t["query"]), torch.empty_like(t["block_table"]), torch.empty_like(
+            t["context_lens"])
+        n_e2e = max(min(args.steps // 5, 2000), 10)
+
+        def e2e_step():
+            dq.copy_(hq, non_blocking=True)
+            dbt.copy_(hbt, non_blocking=True)
+            dctx.copy_(hctx, non_blocking=True)
+            cb.paged_decode(dq, t["kv_pool"], dbt, dctx, num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
+                            out=out, num_physical_blocks=wl.num_blocks)
+            hout.copy_(out, non_blocking=True)
+
+        for _ in range(5):
+            e2e_step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(n_e2e):
+            e2e_step()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        e_ms = a.elapsed_time(b) / n_e2e
+        if world > 1:
+            tt = torch.tensor([e_ms], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            e_ms = float(tt.item())
+        h2d = hq.numel() * hq.element_size() + hbt.numel() * 4 + hctx.numel() * 4
+        d2h = hout.numel() * hout.element_size()
+        e2e = {"value": world * kv_bytes_rank / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "api": "cottus_paged_decode (C ABI via ctypes)"}
+
+    if pool_snapshot is not None:
+        t["kv_pool"].copy_(pool_snapshot)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            r, threads, sample = cpu_reference_rate(w, t, target_s=8.0,
+                                                    max_seqs=1 if w.name == "long_ctx_70b" else None)
+            cpu = {"value": r, "unit": "GB/s", "cores": threads, "kind": "reference", "sample": sample}
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {ex}"}
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peak, peak_kind = peaks()
+    total_kv = (w.kv_bytes() if split else kv_bytes_rank * world)
+    value = total_kv / (ms * 1e-3) / 1e9
+    alg = kv_bytes_rank + wl.io_bytes()
+    achieved = alg / (k_ms * 1e-3) / 1e9
+    traffic = None
+    prof = ROOT / "profiles" / "traffic.json"
+    if prof.exists():
+        traffic = json.loads(prof.read_text()).get(w.name)
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if split else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,1) KV stored via the reference's truncating fp16 encoder",
+        "config": {"workload": describe(w), "kv": "fp16", "q_out": str(w.q_dtype).replace("torch.", ""),
+                   "per_gpu_batch": wl.B, "kv_bytes_per_step_per_gpu": kv_bytes_rank,
+                   "l2": ("L2 flushed between steps (2x L2 buffer written)" if small else
+                          f"inputs larger than L2 ({kv_bytes_rank / 1e6:.0f} MB KV per GPU vs 126 MB L2), no flush"),
+                   "parallelism": (f"split-KV over {world} GPUs, NCCL all-gather of LSE partials" if split else
+                                   f"sequence-sharded over {world} GPU(s), no collective")},
+        "tokens_per_s": w.B * (1 if split else world) / (ms * 1e-3),
+        "pct_hbm_peak": value / world / peak * 100 if not split else value / world / peak * 100,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": "decode_tma_kernel + split_combine_kernel (one cottus_paged_decode call)",
+                     "kernel_ms": k_ms, "algorithmic_bytes": alg},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

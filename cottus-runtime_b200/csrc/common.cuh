@@ -1,0 +1,178 @@
+// Device-side building blocks shared by the cottus_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cottus_b200.h"
+
+namespace cb200 {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Cycles a kernel waits on one barrier before it gives up and reports
+// COTTUS_STATUS_TIMEOUT (about 1 s at the B200 boost clock).
+constexpr long long kWaitLimitCycles = 2000000000LL;
+
+// ---------------------------------------------------------------------------
+// fp16 <-> fp32
+// ---------------------------------------------------------------------------
+
+// fp32 -> fp16 bits by truncation, the KV-cache encoder of the reference
+// (generic_transformer.cpp:255-262): mantissa truncated, biased exponent
+// <= 0 -> signed zero, >= 31 (including inf and NaN) -> signed inf.
+__device__ __forceinline__ uint16_t f32_to_f16_trunc(float f) {
+    uint32_t bits = __float_as_uint(f);
+    uint32_t sign = (bits & 0x80000000u) >> 16;
+    int32_t e = (int32_t)((bits >> 23) & 0xFFu) - 112;
+    uint32_t m = (bits & 0x007FFFFFu) >> 13;
+    uint32_t r = e <= 0 ? sign : (e >= 31 ? (sign | 0x7C00u) : (sign | ((uint32_t)e << 10) | m));
+    return (uint16_t)r;
+}
+
+__device__ __forceinline__ float2 h2_to_f2(uint32_t x) {
+    __half2 h = *reinterpret_cast<__half2*>(&x);
+    return __half22float2(h);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+// Loads 8 consecutive elements (16 B of fp16 or 32 B of fp32) as fp32.
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+    float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void load8(const __half* p, float (&v)[8]) {
+    uint4 r = __ldg(reinterpret_cast<const uint4*>(p));
+    float2 f;
+    f = h2_to_f2(r.x); v[0] = f.x; v[1] = f.y;
+    f = h2_to_f2(r.y); v[2] = f.x; v[3] = f.y;
+    f = h2_to_f2(r.z); v[4] = f.x; v[5] = f.y;
+    f = h2_to_f2(r.w); v[6] = f.x; v[7] = f.y;
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(v[0], v[1], v[2], v[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ void store8(__half* p, const float (&v)[8]) {
+    uint4 r;
+    r.x = pack_h2(v[0], v[1]);
+    r.y = pack_h2(v[2], v[3]);
+    r.z = pack_h2(v[4], v[5]);
+    r.w = pack_h2(v[6], v[7]);
+    *reinterpret_cast<uint4*>(p) = r;
+}
+
+// ---------------------------------------------------------------------------
+// Packed fp32x2 arithmetic (sm_100 FFMA2 / FMUL2)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    unsigned long long ra = *reinterpret_cast<unsigned long long*>(&a);
+    unsigned long long rb = *reinterpret_cast<unsigned long long*>(&b);
+    unsigned long long rc = *reinterpret_cast<unsigned long long*>(&c);
+    unsigned long long rd;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(rd) : "l"(ra), "l"(rb), "l"(rc));
+    return *reinterpret_cast<float2*>(&rd);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    unsigned long long ra = *reinterpret_cast<unsigned long long*>(&a);
+    unsigned long long rb = *reinterpret_cast<unsigned long long*>(&b);
+    unsigned long long rd;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(rd) : "l"(ra), "l"(rb));
+    return *reinterpret_cast<float2*>(&rd);
+}
+
+// ---------------------------------------------------------------------------
+// RoPE rotation of one interleaved pair without FMA contraction
+// (compute_primitives_cpu.cpp:69-71 evaluated in plain fp32, as the
+// reference's -O3 x86-64 build does).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void rope_pair(float x0, float x1, float c, float s, float& o0, float& o1) {
+    o0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
+    o1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier + TMA (cp.async.bulk.tensor) wrappers.  No multicast anywhere.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Waits for phase `parity` of `bar` to complete; gives up after
+// kWaitLimitCycles and returns false (the caller reports a timeout).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitLimitCycles) return false;
+    }
+    return true;
+}
+// 3-D tiled TMA load into this CTA's shared memory, completion counted on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                           int c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
+        : "memory");
+}
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void report(uint32_t* status, uint32_t bits) {
+    if (status) atomicOr(status, bits);
+}
+
+__device__ __forceinline__ int32_t div_up(int32_t a, int32_t b) { return (a + b - 1) / b; }
+
+}  // namespace cb200

@@ -1,0 +1,702 @@
+// Paged decode attention, sm_100a fast path.
+//
+// Work decomposition (stream-K over pages): a unit is one 16-token page of
+// one (sequence, kv head) pair; units are ordered sequence-major, then kv
+// head, then page.  Every warp of the persistent grid is a worker that owns
+// an equal contiguous range of units, so skewed (ragged) batches and long
+// contexts balance exactly across the 148 SMs.
+//
+// Per warp: a ring of RING shared-memory slots, each holding the K and V
+// tiles (2 x 16 rows x head_dim fp16) of one page for one kv head, filled
+// by a single 3-D TMA load (the K and V rows of a page/layer are adjacent
+// in the pool) with completion on an mbarrier; lane 0 refills a slot as
+// soon as the warp has consumed it, so RING-1 pages are always in flight.
+//
+// Math per page: each lane owns 8 consecutive dims of a K/V row (16-byte
+// shared loads, conflict-free), keeps the G query rows of the GQA group in
+// registers (so each KV byte is read from HBM once per group), computes
+// partial dot products with packed fp32x2 FMAs, and reduces them across the
+// D/8 lanes of a row with a transpose-reduce (each shuffle level halves the
+// values a lane holds).  After the reduction every lane holds the scores of
+// ONE head, so the online-softmax max needs only log2(32/G) shuffles.
+// Softmax runs in the log2 domain; the running max is only raised when a
+// new score exceeds it by more than 8 (so exp2 arguments stay <= 8 and the
+// accumulator rescale is rare).  Probabilities go through a per-warp
+// shared scratch to the P.V product, again with packed FMAs.
+//
+// A worker writes a finished (sequence, kv head) pair straight to `out`;
+// a pair cut by a worker boundary leaves (m, l, o) partials in the
+// workspace, merged afterwards by split_combine_kernel.
+//
+// The reference computes the same function per sequence and head with two
+// passes over K (paged_attention_cpu.cpp:53-103); results agree to fp32
+// rounding (summation order and exp2-vs-exp differ).
+#pragma once
+
+#include "common.cuh"
+#include "internal.h"
+
+namespace cb200 {
+
+constexpr int kBS = 16;   // tokens per page on the fast path
+constexpr int kNW = 4;    // worker warps per CTA
+
+struct TmaArgs {
+    void* out;
+    const void* q;
+    const int32_t* bt;
+    const int32_t* ctx;
+    const int32_t* positions;
+    float* lse;
+    float* ws_o;
+    float* ws_ml;
+    uint32_t* status;
+    const void* k_new;
+    const void* v_new;
+    const float* cos_sin;
+    void* q_out;
+    uint16_t* kv;
+    long long num_blocks;
+    int B, H, Hkv, L, layer, maxb, max_pos;
+    int q_f16, out_f16;
+    float qscale;  // softmax scale * log2(e)
+};
+
+// Pages of sequence b, or 0 when its context is empty or invalid.
+template <bool ROPE>
+__device__ __forceinline__ int seq_pages(const TmaArgs& a, int b) {
+    int n;
+    if (ROPE) {
+        int pos = a.positions[b];
+        if (pos < 0 || pos >= a.max_pos) return 0;
+        n = pos + 1;
+    } else {
+        n = a.ctx[b];
+    }
+    if (n <= 0 || n > a.maxb * kBS) return 0;
+    return (n + kBS - 1) / kBS;
+}
+template <bool ROPE>
+__device__ __forceinline__ int seq_ctx(const TmaArgs& a, int b) {
+    return ROPE ? a.positions[b] + 1 : a.ctx[b];
+}
+
+template <int D, int G>
+struct TmaCfg {
+    static constexpr int LW = D / 8;          // lanes covering one row
+    static constexpr int RPS = 32 / LW;       // rows per warp step
+    static constexpr int STEPS_MAX = 16 / RPS;
+    static constexpr int STEPS = (32 / G) < STEPS_MAX ? (32 / G) : STEPS_MAX;  // steps per chunk
+    static constexpr int CH = RPS * STEPS;    // tokens per chunk
+    static constexpr int NCH = kBS / CH;      // chunks per page
+    static constexpr int N = G * STEPS;       // partial dot products per lane per chunk
+    static constexpr int NV = N >= LW ? N / LW : 1;  // values per lane after the reduction
+    static constexpr int CL = LW / G;         // lanes per head inside a row group
+    static constexpr int DUP = N >= LW ? 1 : LW / N;
+    static constexpr int SLOT_BYTES = 2 * kBS * D * 2;
+    static_assert(G <= LW, "group larger than lanes per row");
+    static_assert(kBS % CH == 0, "chunk must divide the page");
+};
+
+template <int RING, int D, int G>
+constexpr size_t tma_smem_bytes() {
+    using C = TmaCfg<D, G>;
+    return (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 8 + (size_t)kNW * C::CH * G * 4 +
+           (size_t)kNW * 2 * G * 4 + 128;
+}
+
+// Transpose-reduce: CNT values per lane are summed over the lanes that
+// differ in the bits O, O/2, ..., 1; each level keeps half the values.
+template <int CNT, int O>
+struct TransposeReduce {
+    __device__ __forceinline__ static void run(float* v, int lq) {
+        if constexpr (O > 0) {
+            if constexpr (CNT > 1) {
+                constexpr int H = CNT / 2;
+                const bool upper = (lq & O) != 0;
+#pragma unroll
+                for (int i = 0; i < H; ++i) {
+                    float send = upper ? v[i] : v[i + H];
+                    float keep = upper ? v[i + H] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, O);
+                }
+                TransposeReduce<H, O / 2>::run(v, lq);
+            } else {
+                v[0] += __shfl_xor_sync(0xffffffffu, v[0], O);
+                TransposeReduce<1, O / 2>::run(v, lq);
+            }
+        }
+    }
+};
+
+struct Cursor {
+    int b, h, p, np;
+};
+
+template <bool ROPE>
+__device__ __forceinline__ void cursor_next(Cursor& c, const TmaArgs& a) {
+    if (++c.p == c.np) {
+        c.p = 0;
+        if (++c.h == a.Hkv) {
+            c.h = 0;
+            do {
+                ++c.b;
+                c.np = c.b < a.B ? seq_pages<ROPE>(a, c.b) : 1;
+            } while (c.np == 0);
+        }
+    }
+}
+
+template <int D, int G, int RING, bool ROPE>
+__global__ void __launch_bounds__(kNW * 32)
+    decode_tma_kernel(const __grid_constant__ CUtensorMap kv_map, const TmaArgs a) {
+    using C = TmaCfg<D, G>;
+    constexpr int LW = C::LW, RPS = C::RPS, STEPS = C::STEPS, CH = C::CH, N = C::N, NV = C::NV;
+    constexpr int CL = C::CL, DUP = C::DUP;
+    constexpr unsigned FULL = 0xffffffffu;
+
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grp = lane / LW, lq = lane % LW;
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
+    uint8_t* slots = smem + (size_t)warp * RING * C::SLOT_BYTES;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kNW * RING * C::SLOT_BYTES) + warp * RING;
+    float* p_s = reinterpret_cast<float*>(smem + (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 8) +
+                 warp * CH * G;
+    float* hs = reinterpret_cast<float*>(smem + (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 8 +
+                                         (size_t)kNW * CH * G * 4) +
+                warp * 2 * G;
+
+    if (lane == 0) {
+        if (warp == 0) prefetch_tensormap(&kv_map);
+#pragma unroll
+        for (int r = 0; r < RING; ++r) mbar_init(&bars[r], 1);
+        fence_barrier_init();
+    }
+    __syncwarp();
+
+    // ---- this worker's unit range --------------------------------------
+    long long total_pages = 0;
+    for (int b = lane; b < a.B; b += 32) total_pages += seq_pages<ROPE>(a, b);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total_pages += __shfl_xor_sync(FULL, total_pages, o);
+    const long long U = total_pages * a.Hkv;
+    const long long W = (long long)gridDim.x * kNW;
+    const long long w = (long long)blockIdx.x * kNW + warp;
+    const long long u0 = w * U / W, u1 = (w + 1) * U / W;
+    if (u0 >= u1) return;
+    const int nu = (int)(u1 - u0);
+
+    // locate u0: sequence by warp-wide prefix scan, then kv head and page
+    Cursor cur;
+    {
+        long long base = 0;
+        int found_b = -1;
+        long long found_excl = 0;
+        for (int bb = 0; bb < a.B && found_b < 0; bb += 32) {
+            const int b = bb + lane;
+            const long long units = b < a.B ? (long long)seq_pages<ROPE>(a, b) * a.Hkv : 0;
+            long long incl = units;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                long long t = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += t;
+            }
+            incl += base;
+            const long long excl = incl - units;
+            const unsigned hit = __ballot_sync(FULL, units > 0 && excl <= u0 && u0 < incl);
+            if (hit) {
+                const int src = __ffs(hit) - 1;
+                found_b = bb + src;
+                found_excl = __shfl_sync(FULL, excl, src);
+            }
+            base = __shfl_sync(FULL, incl, 31);
+        }
+        const int np = seq_pages<ROPE>(a, found_b);
+        const long long r = u0 - found_excl;
+        cur.b = found_b;
+        cur.np = np;
+        cur.h = (int)(r / np);
+        cur.p = (int)(r % np);
+    }
+
+    // ---- TMA issue -------------------------------------------------------
+    auto issue = [&](int k, const Cursor& c) {
+        if (lane == 0) {
+            const int slot = k % RING;
+            const int blk = a.bt[(long long)c.b * a.maxb + c.p];
+            if (blk < 0 || (long long)blk >= a.num_blocks) {
+                mbar_arrive(&bars[slot]);  // nothing to load; the consumer masks the page
+            } else {
+                mbar_arrive_expect_tx(&bars[slot], C::SLOT_BYTES);
+                tma_load_3d(slots + (size_t)slot * C::SLOT_BYTES, &kv_map, &bars[slot], 0, c.h,
+                            (blk * a.L + a.layer) * (2 * kBS));
+            }
+        }
+    };
+    Cursor ic = cur;
+    const int prime = nu < RING ? nu : RING;
+    for (int k = 0; k < prime; ++k) {
+        issue(k, ic);
+        cursor_next<ROPE>(ic, a);
+    }
+
+    float2 q2[G][4];
+    float2 o2[G][4];
+    float m_run = -INFINITY, l_own = 0.f;
+    bool seg_open = false;
+    int seg_start_p = 0;
+    bool seg_first = true;
+    const int i0 = (lq * N) / LW;   // first partial index this lane holds after the reduction
+    const int gl = i0 / STEPS;      // the head this lane scores
+
+    for (int k = 0; k < nu; ++k) {
+        const int slot = k % RING;
+        const int ctx_b = seq_ctx<ROPE>(a, cur.b);
+        if (!seg_open) {
+            // ---- segment start: load (and rotate) the group's query rows ----
+            seg_open = true;
+            seg_first = (k == 0);
+            seg_start_p = cur.p;
+            m_run = -INFINITY;
+            l_own = 0.f;
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const long long row = ((long long)cur.b * a.H + (long long)cur.h * G + g) * D + lq * 8;
+                float x[8];
+                if (a.q_f16) load8(reinterpret_cast<const __half*>(a.q) + row, x);
+                else load8(reinterpret_cast<const float*>(a.q) + row, x);
+                if (ROPE) {
+                    const float4* cs = reinterpret_cast<const float4*>(
+                        a.cos_sin + ((long long)(ctx_b - 1) * (D / 2) + lq * 4) * 2);
+#pragma unroll
+                    for (int pr = 0; pr < 2; ++pr) {
+                        const float4 c4 = __ldg(cs + pr);
+                        rope_pair(x[4 * pr], x[4 * pr + 1], c4.x, c4.y, x[4 * pr], x[4 * pr + 1]);
+                        rope_pair(x[4 * pr + 2], x[4 * pr + 3], c4.z, c4.w, x[4 * pr + 2], x[4 * pr + 3]);
+                    }
+                    if (a.q_out && cur.p == 0 && grp == 0) {
+                        if (a.q_f16) store8(reinterpret_cast<__half*>(a.q_out) + row, x);
+                        else store8(reinterpret_cast<float*>(a.q_out) + row, x);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    q2[g][j] = make_float2(x[2 * j] * a.qscale, x[2 * j + 1] * a.qscale);
+                    o2[g][j] = make_float2(0.f, 0.f);
+                }
+            }
+        }
+
+        const int blk = a.bt[(long long)cur.b * a.maxb + cur.p];
+        const bool blk_ok = blk >= 0 && (long long)blk < a.num_blocks;
+        if (!blk_ok && lane == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
+        int n_valid = blk_ok ? ctx_b - cur.p * kBS : 0;
+        n_valid = n_valid > kBS ? kBS : n_valid;
+
+        const bool landed = __all_sync(FULL, mbar_wait_bounded(&bars[slot], (k / RING) & 1));
+        if (!landed) {
+            if (lane == 0) report(a.status, COTTUS_STATUS_TIMEOUT);
+            // let the loads still in flight land (bounded) before the warp leaves
+            for (int kk = k + 1; kk < k + RING && kk < nu; ++kk)
+                (void)__all_sync(FULL, mbar_wait_bounded(&bars[kk % RING], (kk / RING) & 1));
+            return;
+        }
+        const uint16_t* kt = reinterpret_cast<const uint16_t*>(slots + (size_t)slot * C::SLOT_BYTES);
+        const uint16_t* vt = kt + kBS * D;
+
+        if (ROPE && blk_ok && cur.p == cur.np - 1 && grp == 0) {
+            // ---- the new token: rotate k, encode k and v, append -------------
+            const int t_new = (ctx_b - 1) % kBS;
+            const long long src = ((long long)cur.b * a.Hkv + cur.h) * D + lq * 8;
+            float kx[8], vx[8];
+            if (a.q_f16) {
+                load8(reinterpret_cast<const __half*>(a.k_new) + src, kx);
+                load8(reinterpret_cast<const __half*>(a.v_new) + src, vx);
+            } else {
+                load8(reinterpret_cast<const float*>(a.k_new) + src, kx);
+                load8(reinterpret_cast<const float*>(a.v_new) + src, vx);
+            }
+            const float4* cs =
+                reinterpret_cast<const float4*>(a.cos_sin + ((long long)(ctx_b - 1) * (D / 2) + lq * 4) * 2);
+#pragma unroll
+            for (int pr = 0; pr < 2; ++pr) {
+                const float4 c4 = __ldg(cs + pr);
+                rope_pair(kx[4 * pr], kx[4 * pr + 1], c4.x, c4.y, kx[4 * pr], kx[4 * pr + 1]);
+                rope_pair(kx[4 * pr + 2], kx[4 * pr + 3], c4.z, c4.w, kx[4 * pr + 2], kx[4 * pr + 3]);
+            }
+            uint32_t kw[4], vw[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                kw[j] = (uint32_t)f32_to_f16_trunc(kx[2 * j]) | ((uint32_t)f32_to_f16_trunc(kx[2 * j + 1]) << 16);
+                vw[j] = (uint32_t)f32_to_f16_trunc(vx[2 * j]) | ((uint32_t)f32_to_f16_trunc(vx[2 * j + 1]) << 16);
+            }
+            const uint4 k4 = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+            const uint4 v4 = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+            *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kt) + t_new * D + lq * 8) = k4;
+            *reinterpret_cast<uint4*>(const_cast<uint16_t*>(vt) + t_new * D + lq * 8) = v4;
+            const long long row0 = ((long long)blk * a.L + a.layer) * (2 * kBS);
+            const long long koff = ((row0 + t_new) * a.Hkv + cur.h) * D + lq * 8;
+            const long long voff = ((row0 + kBS + t_new) * a.Hkv + cur.h) * D + lq * 8;
+            *reinterpret_cast<uint4*>(a.kv + koff) = k4;
+            *reinterpret_cast<uint4*>(a.kv + voff) = v4;
+        }
+        if (ROPE) __syncwarp();
+
+        // ---- the page, CH tokens at a time ------------------------------------
+#pragma unroll
+        for (int c = 0; c < C::NCH; ++c) {
+            const int tb = c * CH;
+            float part[N];
+#pragma unroll
+            for (int s = 0; s < STEPS; ++s) {
+                const int row = tb + s * RPS + grp;
+                const uint4 raw = *reinterpret_cast<const uint4*>(kt + row * D + lq * 8);
+                const float2 k0 = h2_to_f2(raw.x), k1 = h2_to_f2(raw.y), k2 = h2_to_f2(raw.z),
+                             k3 = h2_to_f2(raw.w);
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    float2 acc = fmul2(q2[g][0], k0);
+                    acc = ffma2(q2[g][1], k1, acc);
+                    acc = ffma2(q2[g][2], k2, acc);
+                    acc = ffma2(q2[g][3], k3, acc);
+                    part[g * STEPS + s] = acc.x + acc.y;
+                }
+            }
+            TransposeReduce<N, LW / 2>::run(part, lq);
+
+            // scores of this lane (head gl), masked past the context
+            float sc[NV];
+            bool ok[NV];
+            float cmax = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                const int s = (i0 + j) % STEPS;
+                const int t = tb + s * RPS + grp;
+                ok[j] = t < n_valid;
+                sc[j] = ok[j] ? part[j] : -INFINITY;
+                cmax = fmaxf(cmax, sc[j]);
+            }
+#pragma unroll
+            for (int o = 1; o < CL; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(FULL, cmax, o));
+#pragma unroll
+            for (int o = LW; o < 32; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(FULL, cmax, o));
+
+            const bool upd = cmax > m_run + 8.0f;
+            if (__any_sync(FULL, upd)) {
+                const float m_new = upd ? cmax : m_run;
+                const float alpha = upd ? exp2f(m_run - m_new) : 1.0f;
+                l_own *= alpha;
+                m_run = m_new;
+                if (grp == 0 && (lq % CL) == 0) hs[gl] = alpha;
+                __syncwarp();
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float al = hs[g];
+                    const float2 al2 = make_float2(al, al);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) o2[g][j] = fmul2(o2[g][j], al2);
+                }
+                __syncwarp();
+            }
+            float psum = 0.f;
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+                const float pj = ok[j] ? exp2f(sc[j] - m_run) : 0.f;
+                psum += pj;
+                const int s = (i0 + j) % STEPS;
+                p_s[(grp * STEPS + s) * G + gl] = pj;
+            }
+            if (DUP == 1 || (lq % DUP) == 0) l_own += psum;
+            __syncwarp();
+
+#pragma unroll
+            for (int s = 0; s < STEPS; ++s) {
+                const int row = tb + s * RPS + grp;
+                uint4 raw = *reinterpret_cast<const uint4*>(vt + row * D + lq * 8);
+                if (row >= n_valid) raw = make_uint4(0u, 0u, 0u, 0u);
+                const float2 v0 = h2_to_f2(raw.x), v1 = h2_to_f2(raw.y), v2 = h2_to_f2(raw.z),
+                             v3 = h2_to_f2(raw.w);
+                float pv[G];
+#pragma unroll
+                for (int g = 0; g < G; ++g) pv[g] = p_s[(grp * STEPS + s) * G + g];
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float2 p2 = make_float2(pv[g], pv[g]);
+                    o2[g][0] = ffma2(p2, v0, o2[g][0]);
+                    o2[g][1] = ffma2(p2, v1, o2[g][1]);
+                    o2[g][2] = ffma2(p2, v2, o2[g][2]);
+                    o2[g][3] = ffma2(p2, v3, o2[g][3]);
+                }
+            }
+            __syncwarp();
+        }
+
+        // ---- refill this slot --------------------------------------------
+        if (k + RING < nu) {
+            fence_proxy_async_smem();
+            issue(k + RING, ic);
+            cursor_next<ROPE>(ic, a);
+        }
+
+        // ---- segment end -------------------------------------------------
+        const bool seg_end = (cur.p == cur.np - 1) || (k == nu - 1);
+        if (seg_end) {
+#pragma unroll
+            for (int o = LW; o < 32; o <<= 1) {
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        o2[g][j].x += __shfl_xor_sync(FULL, o2[g][j].x, o);
+                        o2[g][j].y += __shfl_xor_sync(FULL, o2[g][j].y, o);
+                    }
+                }
+            }
+            float lt = l_own;
+#pragma unroll
+            for (int o = 1; o < CL; o <<= 1) lt += __shfl_xor_sync(FULL, lt, o);
+#pragma unroll
+            for (int o = LW; o < 32; o <<= 1) lt += __shfl_xor_sync(FULL, lt, o);
+            if (grp == 0 && (lq % CL) == 0) {
+                hs[2 * gl] = m_run;
+                hs[2 * gl + 1] = lt;
+            }
+            __syncwarp();
+            const bool whole = seg_start_p == 0 && cur.p == cur.np - 1;
+            if (grp == 0) {
+                const long long slot_id = seg_first ? 2 * w : 2 * w + 1;
+#pragma unroll
+                for (int g = 0; g < G; ++g) {
+                    const float mg = hs[2 * g], lg = hs[2 * g + 1];
+                    const long long head = (long long)cur.b * a.H + (long long)cur.h * G + g;
+                    float x[8];
+                    if (whole) {
+                        const float inv = lg > 0.f ? 1.0f / lg : 0.f;
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            x[2 * j] = o2[g][j].x * inv;
+                            x[2 * j + 1] = o2[g][j].y * inv;
+                        }
+                        if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + head * D + lq * 8, x);
+                        else store8(reinterpret_cast<float*>(a.out) + head * D + lq * 8, x);
+                        if (a.lse && lq == 0) a.lse[head] = lg > 0.f ? (mg + log2f(lg)) * kLn2 : -INFINITY;
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            x[2 * j] = o2[g][j].x;
+                            x[2 * j + 1] = o2[g][j].y;
+                        }
+                        store8(a.ws_o + (slot_id * G + g) * D + lq * 8, x);
+                        if (lq == 0) {
+                            a.ws_ml[(slot_id * G + g) * 2] = mg;
+                            a.ws_ml[(slot_id * G + g) * 2 + 1] = lg;
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            seg_open = false;
+        }
+        if (k + 1 < nu) cursor_next<ROPE>(cur, a);
+    }
+}
+
+// Merges the partials of pairs that were cut by worker boundaries, writes
+// zeros for empty/invalid sequences.  One CTA per sequence.
+template <bool ROPE>
+__global__ void __launch_bounds__(256) split_combine_kernel(const TmaArgs a, int G, int D, long long W) {
+    const int b = blockIdx.x;
+    __shared__ long long red[2][8];
+    long long before = 0, total = 0;
+    for (int bb = threadIdx.x; bb < a.B; bb += blockDim.x) {
+        const long long n = seq_pages<ROPE>(a, bb);
+        total += n;
+        if (bb < b) before += n;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        before += __shfl_xor_sync(0xffffffffu, before, o);
+        total += __shfl_xor_sync(0xffffffffu, total, o);
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+    if (lane == 0) {
+        red[0][warp] = before;
+        red[1][warp] = total;
+    }
+    __syncthreads();
+    before = 0;
+    total = 0;
+    for (int i = 0; i < nwarps; ++i) {
+        before += red[0][i];
+        total += red[1][i];
+    }
+    const int np = seq_pages<ROPE>(a, b);
+    if (np == 0) {
+        const int n = seq_ctx<ROPE>(a, b);
+        if (threadIdx.x == 0 && (n != 0 || ROPE)) report(a.status, ROPE ? COTTUS_STATUS_BAD_POSITION
+                                                                        : COTTUS_STATUS_BAD_CONTEXT);
+        const long long nel = (long long)a.H * D;
+        for (long long i = threadIdx.x; i < nel; i += blockDim.x) {
+            if (a.out_f16) reinterpret_cast<__half*>(a.out)[(long long)b * nel + i] = __float2half_rn(0.f);
+            else reinterpret_cast<float*>(a.out)[(long long)b * nel + i] = 0.f;
+        }
+        if (a.lse)
+            for (int i = threadIdx.x; i < a.H; i += blockDim.x) a.lse[(long long)b * a.H + i] = -INFINITY;
+        return;
+    }
+    const long long U = total * a.Hkv;
+    const long long seq_base = before * a.Hkv;
+    for (int hg = warp; hg < a.Hkv * G; hg += nwarps) {
+        const int h = hg / G, g = hg % G;
+        const long long ps = seq_base + (long long)h * np;
+        const long long pe = ps + np - 1;
+        const long long w0 = ((ps + 1) * W - 1) / U;
+        const long long w1 = ((pe + 1) * W - 1) / U;
+        if (w0 == w1) continue;
+        float M = -INFINITY;
+        for (long long wk = w0; wk <= w1; ++wk) {
+            const long long s0 = wk * U / W, s1 = (wk + 1) * U / W;
+            if (s0 >= s1) continue;
+            const long long slot = s0 >= ps ? 2 * wk : 2 * wk + 1;
+            M = fmaxf(M, a.ws_ml[(slot * G + g) * 2]);
+        }
+        float Ls = 0.f;
+        for (long long wk = w0; wk <= w1; ++wk) {
+            const long long s0 = wk * U / W, s1 = (wk + 1) * U / W;
+            if (s0 >= s1) continue;
+            const long long slot = s0 >= ps ? 2 * wk : 2 * wk + 1;
+            const float m = a.ws_ml[(slot * G + g) * 2];
+            if (m != -INFINITY) Ls += a.ws_ml[(slot * G + g) * 2 + 1] * exp2f(m - M);
+        }
+        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+        const long long head = (long long)b * a.H + (long long)h * G + g;
+        for (int d = lane; d < D; d += 32) {
+            float acc = 0.f;
+            for (long long wk = w0; wk <= w1; ++wk) {
+                const long long s0 = wk * U / W, s1 = (wk + 1) * U / W;
+                if (s0 >= s1) continue;
+                const long long slot = s0 >= ps ? 2 * wk : 2 * wk + 1;
+                const float m = a.ws_ml[(slot * G + g) * 2];
+                if (m != -INFINITY) acc += a.ws_o[(slot * G + g) * D + d] * exp2f(m - M);
+            }
+            acc *= inv;
+            if (a.out_f16) reinterpret_cast<__half*>(a.out)[head * D + d] = __float2half_rn(acc);
+            else reinterpret_cast<float*>(a.out)[head * D + d] = acc;
+        }
+        if (a.lse && lane == 0) a.lse[head] = Ls > 0.f ? (M + log2f(Ls)) * kLn2 : -INFINITY;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Host side of one head_dim: tensor map, occupancy cache, launch.
+// ---------------------------------------------------------------------------
+CUtensorMap make_kv_tensor_map(const DecodeDesc& d, cudaError_t* err);
+int device_sm_count(int device);
+
+template <int D, int G, int RING, bool ROPE>
+struct TmaLauncher {
+    static int blocks_per_sm(int device) {
+        static int cache[64] = {0};
+        if (device < 0 || device >= 64) return 1;
+        if (cache[device] == 0) {
+            auto kern = decode_tma_kernel<D, G, RING, ROPE>;
+            const size_t smem = tma_smem_bytes<RING, D, G>();
+            cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            int n = 0;
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kNW * 32, smem);
+            cache[device] = n > 0 ? n : 1;
+        }
+        return cache[device];
+    }
+    static long long workers(int device) {
+        return (long long)device_sm_count(device) * blocks_per_sm(device) * kNW;
+    }
+    static cudaError_t launch(const DecodeDesc& d, cudaStream_t st) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        const long long W = workers(dev);
+        const int grid = (int)(W / kNW);
+        cudaError_t err = cudaSuccess;
+        const CUtensorMap map = make_kv_tensor_map(d, &err);
+        if (err != cudaSuccess) return err;
+        TmaArgs a;
+        a.out = d.out;
+        a.q = d.q;
+        a.bt = d.block_table;
+        a.ctx = d.context_lens;
+        a.positions = d.positions;
+        a.lse = d.lse;
+        a.ws_o = reinterpret_cast<float*>(d.workspace);
+        a.ws_ml = reinterpret_cast<float*>(d.workspace) + (size_t)2 * W * G * D;
+        a.status = d.status;
+        a.k_new = d.k_new;
+        a.v_new = d.v_new;
+        a.cos_sin = d.cos_sin;
+        a.q_out = d.q_out;
+        a.kv = d.kv_mut;
+        a.num_blocks = d.num_blocks;
+        a.B = d.batch;
+        a.H = d.num_heads;
+        a.Hkv = d.num_kv_heads;
+        a.L = d.num_layers;
+        a.layer = d.layer;
+        a.maxb = d.max_blocks;
+        a.max_pos = d.max_position;
+        a.q_f16 = d.q_f16;
+        a.out_f16 = d.out_f16;
+        a.qscale = d.scale * kLog2e;
+        const size_t smem = tma_smem_bytes<RING, D, G>();
+        decode_tma_kernel<D, G, RING, ROPE><<<grid, kNW * 32, smem, st>>>(map, a);
+        err = cudaGetLastError();
+        if (err != cudaSuccess) return err;
+        split_combine_kernel<ROPE><<<d.batch, 256, 0, st>>>(a, G, D, W);
+        return cudaGetLastError();
+    }
+};
+
+template <int D, int RING>
+cudaError_t dispatch_tma(const DecodeDesc& d, cudaStream_t st) {
+    const int G = d.num_heads / d.num_kv_heads;
+    if (d.rope) {
+        switch (G) {
+            case 1: return TmaLauncher<D, 1, RING, true>::launch(d, st);
+            case 2: return TmaLauncher<D, 2, RING, true>::launch(d, st);
+            case 4: return TmaLauncher<D, 4, RING, true>::launch(d, st);
+            case 8: return TmaLauncher<D, 8, RING, true>::launch(d, st);
+        }
+    } else {
+        switch (G) {
+            case 1: return TmaLauncher<D, 1, RING, false>::launch(d, st);
+            case 2: return TmaLauncher<D, 2, RING, false>::launch(d, st);
+            case 4: return TmaLauncher<D, 4, RING, false>::launch(d, st);
+            case 8: return TmaLauncher<D, 8, RING, false>::launch(d, st);
+        }
+    }
+    return cudaErrorInvalidValue;
+}
+
+template <int D, int RING>
+size_t dispatch_workers(const DecodeDesc& d) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int G = d.num_heads / d.num_kv_heads;
+    if (d.rope) {
+        switch (G) {
+            case 1: return TmaLauncher<D, 1, RING, true>::workers(dev);
+            case 2: return TmaLauncher<D, 2, RING, true>::workers(dev);
+            case 4: return TmaLauncher<D, 4, RING, true>::workers(dev);
+            case 8: return TmaLauncher<D, 8, RING, true>::workers(dev);
+        }
+    } else {
+        switch (G) {
+            case 1: return TmaLauncher<D, 1, RING, false>::workers(dev);
+            case 2: return TmaLauncher<D, 2, RING, false>::workers(dev);
+            case 4: return TmaLauncher<D, 4, RING, false>::workers(dev);
+            case 8: return TmaLauncher<D, 8, RING, false>::workers(dev);
+        }
+    }
+    return 0;
+}
+
+}  // namespace cb200

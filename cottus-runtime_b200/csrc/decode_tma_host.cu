@@ -1,0 +1,105 @@
+// Host side of the TMA fast path: support predicate, workspace size,
+// KV-pool tensor map, per-device SM count, dispatch by head_dim.
+#include <cudaTypedefs.h>
+
+#include <cstring>
+#include <mutex>
+
+#include "decode_tma.cuh"
+
+namespace cb200 {
+
+int device_sm_count(int device) {
+    static int cache[64] = {0};
+    if (device < 0 || device >= 64) return 148;
+    if (cache[device] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+        cache[device] = n > 0 ? n : 148;
+    }
+    return cache[device];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// View of the pool as rows of head_dim fp16 values:
+//   dim0 = head_dim (contiguous), dim1 = kv head (stride head_dim),
+//   dim2 = (block, layer, K|V, token) rows (stride num_kv_heads*head_dim).
+// One 16 x 2 box row range of dim2 covers the K rows then the V rows of a
+// page/layer, so box {head_dim, 1, 32} loads both tiles of one kv head.
+CUtensorMap make_kv_tensor_map(const DecodeDesc& d, cudaError_t* err) {
+    CUtensorMap map;
+    std::memset(&map, 0, sizeof map);
+    auto fn = encode_fn();
+    if (!fn) {
+        *err = cudaErrorNotSupported;
+        return map;
+    }
+    const void* base = d.rope ? static_cast<const void*>(d.kv_mut) : static_cast<const void*>(d.kv);
+    cuuint64_t dims[3] = {(cuuint64_t)d.head_dim, (cuuint64_t)d.num_kv_heads,
+                          (cuuint64_t)d.num_blocks * d.num_layers * 2 * kBS};
+    cuuint64_t strides[2] = {(cuuint64_t)d.head_dim * 2, (cuuint64_t)d.num_kv_heads * d.head_dim * 2};
+    cuuint32_t box[3] = {(cuuint32_t)d.head_dim, 1, 2 * kBS};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    *err = r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+    return map;
+}
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+bool tma_supported(const DecodeDesc& d) {
+    if (d.block_size != kBS) return false;
+    if (d.head_dim != 64 && d.head_dim != 128 && d.head_dim != 256) return false;
+    if (d.num_kv_heads <= 0 || d.num_heads % d.num_kv_heads != 0) return false;
+    const int G = d.num_heads / d.num_kv_heads;
+    if (G != 1 && G != 2 && G != 4 && G != 8) return false;
+    const void* pool = d.rope ? static_cast<const void*>(d.kv_mut) : static_cast<const void*>(d.kv);
+    if (!aligned16(pool) || !aligned16(d.q) || !aligned16(d.out)) return false;
+    if (d.rope && (!d.cos_sin || !aligned16(d.k_new) || !aligned16(d.v_new) || !aligned16(d.q_out) ||
+                   !aligned16(d.cos_sin)))
+        return false;
+    if (d.num_blocks <= 0 || d.num_blocks * (int64_t)d.num_layers * 2 * kBS >= (int64_t(1) << 31)) return false;
+    if ((int64_t)d.batch * d.num_heads >= (int64_t(1) << 31)) return false;
+    return true;
+}
+
+static size_t workers(const DecodeDesc& d) {
+    switch (d.head_dim) {
+        case 64: return tma_workers_d64(d);
+        case 128: return tma_workers_d128(d);
+        case 256: return tma_workers_d256(d);
+    }
+    return 0;
+}
+
+size_t tma_workspace_bytes(const DecodeDesc& d) {
+    const size_t W = workers(d);
+    const size_t G = (size_t)(d.num_heads / d.num_kv_heads);
+    return 2 * W * G * ((size_t)d.head_dim + 2) * sizeof(float) + 256;
+}
+
+cudaError_t launch_decode_tma(const DecodeDesc& d, cudaStream_t st) {
+    switch (d.head_dim) {
+        case 64: return launch_decode_tma_d64(d, st);
+        case 128: return launch_decode_tma_d128(d, st);
+        case 256: return launch_decode_tma_d256(d, st);
+    }
+    return cudaErrorInvalidValue;
+}
+
+}  // namespace cb200

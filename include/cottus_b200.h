@@ -1,0 +1,219 @@
+/*
+ * cottus_b200 — B200 (sm_100a) decode hot path of cottus-runtime behind a C ABI.
+ *
+ * Paged decode attention over the BlockAllocator / PageTable fp16 KV cache,
+ * the fused RoPE + KV-cache append that feeds it, the split-KV
+ * log-sum-exp merge, and the host-side block pool.  Plain pointers and
+ * sizes only; every device pointer is caller-owned; nothing here allocates
+ * device memory per call (split-KV scratch is a caller-provided workspace).
+ * Calls are stream-ordered and never synchronise the device, except the
+ * host-side helpers marked "host".
+ *
+ * Citations are to the cottus-runtime sources (path:line from the project
+ * root).
+ *
+ * KV pool layout (identical to the reference, paged_attention_cpu.cpp:45-46,
+ * 63-67, 88-92; tests/test_kv_layout_hardening.cpp:6-35):
+ *   uint16 fp16 bit patterns
+ *   [num_physical_blocks][num_layers][K|V][block_size][num_kv_heads][head_dim]
+ * GQA map (paged_attention_cpu.cpp:48): kv_head(h) = h * num_kv_heads / num_heads.
+ */
+#ifndef COTTUS_B200_H
+#define COTTUS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same type as cudaStream_t; NULL is the legacy default stream. */
+typedef struct CUstream_st *cottus_stream_t;
+
+/* Return codes.  The reference throws; the ABI never does. */
+enum cottus_status {
+    COTTUS_OK = 0,
+    COTTUS_ERR_INVALID_ARGUMENT = -1, /* std::invalid_argument (paged_attention_cuda.cu:109-113) */
+    COTTUS_ERR_OUT_OF_RANGE = -2,     /* std::out_of_range (page_table.cpp:18-26, generic_transformer.cpp:224-226) */
+    COTTUS_ERR_CUDA = -3,             /* std::runtime_error("CUDA error: ...") (paged_attention_cuda.cu:8-14) */
+    COTTUS_ERR_UNSUPPORTED = -4,      /* shape outside what the kernels implement */
+    COTTUS_ERR_WORKSPACE = -5,        /* split-KV workspace missing or too small */
+    COTTUS_ERR_OUT_OF_MEMORY = -6,    /* BlockAllocator "Out of memory" (block_allocator.cpp:23-25) */
+    COTTUS_ERR_DOUBLE_FREE = -7       /* BlockAllocator "Double free detected" (block_allocator.cpp:38-40) */
+};
+
+/* Bits OR-ed into the optional device status word by the kernels.  Device
+ * checks cannot throw; they zero the affected output rows and set a bit. */
+#define COTTUS_STATUS_BAD_BLOCK_ID 0x1u /* block id outside [0, num_physical_blocks) */
+#define COTTUS_STATUS_BAD_CONTEXT 0x2u  /* context < 0 or > max_blocks_per_seq * block_size */
+#define COTTUS_STATUS_BAD_POSITION 0x4u /* position outside the table / RoPE cache */
+#define COTTUS_STATUS_TIMEOUT 0x8u      /* a bounded wait inside a kernel gave up */
+
+enum cottus_dtype { COTTUS_F32 = 0, COTTUS_F16 = 1 };
+
+/* Message of the last error returned on this host thread (mirrors the
+ * reference's exception text where one exists). */
+const char *cottus_last_error(void);
+const char *cottus_status_string(int status);
+int cottus_version(void);
+
+/* ------------------------------------------------------------------------
+ * Batched paged decode attention.
+ * Replaces cottus::pagedAttentionCUDA (paged_attention_cuda.h:9-21,
+ * paged_attention_cuda.cu:96-149) and its CPU twin cottus::pagedAttentionCPU
+ * (paged_attention_cpu.h:8-20): one query token per sequence, a whole batch
+ * per call, device-resident pool and block table, caller's stream.
+ * For each sequence b and query head h:
+ *   out[b][h] = softmax(scale * q[b][h] . K_b^T) V_b over the first
+ *   context_lens[b] tokens of sequence b, K_b/V_b gathered through
+ *   block_table[b][:] from layer `layer` of the pool.
+ * context_lens[b] == 0 writes zeros (an idle batch slot); the reference has
+ * no batch and rejects seqLen <= 0.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    void *out;                  /* [batch][num_heads][head_dim], out_dtype */
+    const void *query;          /* [batch][num_heads][head_dim], q_dtype */
+    const uint16_t *kv_pool;    /* fp16 bit patterns, layout above */
+    const int32_t *block_table; /* [batch][max_blocks_per_seq] physical block ids */
+    const int32_t *context_lens;/* [batch] tokens per sequence */
+    int64_t num_physical_blocks;
+    int32_t batch;
+    int32_t num_heads;
+    int32_t num_kv_heads;
+    int32_t head_dim;
+    int32_t block_size;
+    int32_t num_layers;
+    int32_t layer;
+    int32_t max_blocks_per_seq;
+    int32_t q_dtype;            /* enum cottus_dtype */
+    int32_t out_dtype;          /* enum cottus_dtype */
+    float scale;                /* <= 0 selects 1/sqrt(head_dim) (paged_attention_cpu.cpp:75) */
+    /* Optional split-KV partial mode: when non-NULL, `out` receives the
+     * normalised partial output and lse_out[b][h] its natural-log
+     * log-sum-exp, for cottus_lse_combine across context shards. */
+    float *lse_out;
+    void *workspace;            /* >= cottus_paged_decode_workspace_size() bytes, 256-B aligned */
+    size_t workspace_bytes;
+    uint32_t *status;           /* optional device word, COTTUS_STATUS_* bits */
+} cottus_paged_decode_params;
+
+/* Scratch bytes that cottus_paged_decode needs for these parameters on the
+ * current device (independent of the context lengths).  0 means none. */
+size_t cottus_paged_decode_workspace_size(const cottus_paged_decode_params *p);
+int cottus_paged_decode(const cottus_paged_decode_params *p, cottus_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Split-KV merge of partial (normalised output, log-sum-exp) pairs produced
+ * over disjoint context shards (e.g. one per GPU):
+ *   lse = log(sum_i exp(lse_i));  out = sum_i exp(lse_i - lse) * out_i.
+ * No reference counterpart (the reference never splits a context); its
+ * result equals the un-split cottus::pagedAttentionCPU output.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    void *out;                /* [batch][num_heads][head_dim], out_dtype */
+    float *lse_out;           /* optional [batch][num_heads] */
+    const float *partial_out; /* [num_parts][batch][num_heads][head_dim] */
+    const float *partial_lse; /* [num_parts][batch][num_heads]; -inf marks an empty shard */
+    int32_t num_parts;
+    int32_t batch;
+    int32_t num_heads;
+    int32_t head_dim;
+    int32_t out_dtype;
+} cottus_lse_combine_params;
+
+int cottus_lse_combine(const cottus_lse_combine_params *p, cottus_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * RoPE.  Replaces cottus::ropeCUDA / ropeCPU (compute_primitives_cuda.h:22-29,
+ * compute_primitives_cpu.cpp:46-73): interleaved pairs (2d, 2d+1),
+ *   out0 = x0*cos - x1*sin,  out1 = x0*sin + x1*cos,
+ * angle = pos / theta^(2d/head_dim).  The (cos, sin) values come from a
+ * table filled on the host with the reference's float formula, and the
+ * rotation is evaluated without fused multiply-adds, so results are
+ * bit-identical to ropeCPU.
+ * ---------------------------------------------------------------------- */
+
+/* host: table[max_position][head_dim/2][2] = (cos, sin), reference formula. */
+int cottus_rope_cos_sin_fill(float *host_table, int32_t max_position, int32_t head_dim, float theta);
+
+/* x[num_tokens][num_heads][head_dim] fp32, in place allowed; positions[t]
+ * is token t's position; cos_sin: device table from cottus_rope_cos_sin_fill. */
+int cottus_rope(float *out, const float *in, const int32_t *positions, int32_t num_tokens, int32_t num_heads,
+                int32_t head_dim, const float *cos_sin, int32_t max_position, cottus_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * One decode step of one layer: RoPE on the new token's q and k, KV append
+ * (fp32 -> fp16 by truncation, subnormal results flushed to signed zero,
+ * overflow/NaN -> signed inf; written to slot positions[b] % block_size of
+ * block block_table[b][positions[b] / block_size]), optionally followed by
+ * paged attention over positions[b] + 1 tokens, in one kernel.
+ * Replaces generic_transformer.cpp:196-291 (ropeCUDA x2, the host-side
+ * encode/scatter loop and pagedAttentionCUDA).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const void *query;          /* [batch][num_heads][head_dim], qkv_dtype (not yet rotated) */
+    const void *key;            /* [batch][num_kv_heads][head_dim], qkv_dtype (not yet rotated) */
+    const void *value;          /* [batch][num_kv_heads][head_dim], qkv_dtype */
+    int32_t qkv_dtype;          /* enum cottus_dtype */
+    const int32_t *positions;   /* [batch] position of the new token */
+    const float *cos_sin;       /* device [max_position][head_dim/2][2]; NULL = no rotation */
+    int32_t max_position;
+    uint16_t *kv_pool;
+    const int32_t *block_table; /* [batch][max_blocks_per_seq] */
+    int64_t num_physical_blocks;
+    int32_t batch;
+    int32_t num_heads;
+    int32_t num_kv_heads;
+    int32_t head_dim;
+    int32_t block_size;
+    int32_t num_layers;
+    int32_t layer;
+    int32_t max_blocks_per_seq;
+    void *query_out;            /* optional rotated query, qkv_dtype, [batch][num_heads][head_dim] */
+    /* attention part (cottus_rope_append_decode only) */
+    void *out;                  /* [batch][num_heads][head_dim], out_dtype */
+    int32_t out_dtype;
+    float scale;                /* <= 0: 1/sqrt(head_dim) */
+    void *workspace;
+    size_t workspace_bytes;
+    uint32_t *status;           /* optional device word */
+} cottus_decode_step_params;
+
+/* RoPE + append only (no attention; `out`, `workspace` ignored). */
+int cottus_rope_append(const cottus_decode_step_params *p, cottus_stream_t stream);
+/* RoPE + append + paged attention over positions[b] + 1 tokens. */
+size_t cottus_rope_append_decode_workspace_size(const cottus_decode_step_params *p);
+int cottus_rope_append_decode(const cottus_decode_step_params *p, cottus_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Block-table gather: copies, bit for bit, the K and V rows of layer
+ * `layer` for the first context_lens[b] tokens of each sequence into dense
+ * k_out/v_out [batch][max_context][num_kv_heads][head_dim] (fp16 bits);
+ * rows past a sequence's context are left untouched.  This is the gather of
+ * paged_attention_cpu.cpp:53-67,86-92 (and paged_attention_cuda.cu:131-135)
+ * exposed on its own.
+ * ---------------------------------------------------------------------- */
+int cottus_paged_gather(uint16_t *k_out, uint16_t *v_out, const uint16_t *kv_pool, const int32_t *block_table,
+                        const int32_t *context_lens, int64_t num_physical_blocks, int32_t batch,
+                        int32_t max_context, int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                        int32_t num_layers, int32_t layer, int32_t max_blocks_per_seq, uint32_t *status,
+                        cottus_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * host: LIFO block pool, cottus::BlockAllocator (block_allocator.h:9-14,
+ * block_allocator.cpp:7-55).  The first allocation returns block 0.
+ * ---------------------------------------------------------------------- */
+typedef struct cottus_block_allocator cottus_block_allocator;
+int cottus_block_allocator_create(int32_t total_blocks, int32_t block_size, cottus_block_allocator **out);
+void cottus_block_allocator_destroy(cottus_block_allocator *a);
+int cottus_block_allocator_allocate(cottus_block_allocator *a, int32_t *block_id);
+int cottus_block_allocator_free(cottus_block_allocator *a, int32_t block_id);
+int32_t cottus_block_allocator_num_free(const cottus_block_allocator *a);
+int32_t cottus_block_allocator_total_blocks(const cottus_block_allocator *a);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* COTTUS_B200_H */

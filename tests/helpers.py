@@ -1,0 +1,57 @@
+"""Shared test helpers: run the oracle on (a subset of) a device workload,
+and a plain torch fp32 attention reference for full-size checks."""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from cottus_b200.workloads import host_subpool  # noqa: F401  (re-exported for tests)
+
+TOL_F32 = 1e-5   # max-abs error bound for fp32 outputs
+TOL_F16 = 2e-3   # max-abs error bound for fp16 outputs
+
+
+def tol_for(dtype) -> float:
+    return TOL_F32 if dtype == torch.float32 else TOL_F16
+
+
+def oracle_outputs(oracle, w, t, seqs, query=None):
+    """Oracle (C restatement of pagedAttentionCPU) outputs for `seqs`."""
+    seqs = list(seqs)
+    sub, bt, ctx = host_subpool(w, t["kv_pool"], seqs)
+    q = (t["query"] if query is None else query)[seqs].float().cpu().numpy()
+    return oracle.paged_attention_batch(q, sub, bt, ctx, w.layer, w.H, w.Hkv, w.D, w.bs, w.L)
+
+
+def torch_reference(w, t, query=None, seqs=None):
+    """fp32 attention on the GPU from a dense torch gather of the pages."""
+    per = w.block_elems()
+    pool = t["kv_pool"].view(-1, w.L, 2, w.bs, w.Hkv, w.D)[:, w.layer]
+    q = (t["query"] if query is None else query).float()
+    G = w.H // w.Hkv
+    scale = 1.0 / np.sqrt(w.D)
+    outs = []
+    seqs = range(w.B) if seqs is None else seqs
+    bt = torch.from_numpy(w.block_table).to(pool.device).long()
+    for b in seqs:
+        n = int(w.ctx[b])
+        if n == 0:
+            outs.append(torch.zeros(w.H, w.D, device=pool.device))
+            continue
+        pages = (n + w.bs - 1) // w.bs
+        blk = pool.index_select(0, bt[b, :pages])                  # [pages, 2, bs, Hkv, D]
+        k = blk[:, 0].reshape(-1, w.Hkv, w.D)[:n].view(torch.float16).float()
+        v = blk[:, 1].reshape(-1, w.Hkv, w.D)[:n].view(torch.float16).float()
+        kq = k.repeat_interleave(G, dim=1)                        # [n, H, D]
+        vq = v.repeat_interleave(G, dim=1)
+        s = torch.einsum("hd,nhd->hn", q[b], kq) * scale
+        p = torch.softmax(s, dim=-1)
+        outs.append(torch.einsum("hn,nhd->hd", p, vq))
+    _ = per
+    return torch.stack(outs)
+
+
+def max_abs(a, b) -> float:
+    a = a.float().cpu().numpy() if isinstance(a, torch.Tensor) else np.asarray(a, np.float32)
+    b = b.float().cpu().numpy() if isinstance(b, torch.Tensor) else np.asarray(b, np.float32)
+    return float(np.max(np.abs(a.astype(np.float64) - b.astype(np.float64)))) if a.size else 0.0
