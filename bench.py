@@ -129,11 +129,12 @@ def cpu_reference_rate(w, t, target_s=8.0, max_seqs=None):
 
 # -- main --------------------------------------------------------------------------------------
 
-def build_workload(name, rank):
+def build_workload(name, rank, batch=None):
     from cottus_b200 import workloads as W
 
     seed = 1000 + rank
-    return W.BUILDERS[name](seed=seed)
+    kw = {"B": batch} if batch else {}
+    return W.BUILDERS[name](seed=seed, **kw)
 
 
 def run_reference(args, rank, world):
@@ -142,7 +143,7 @@ def run_reference(args, rank, world):
     if world > 1 and rank != 0:
         return
     from cottus_b200 import workloads as W
-    w = build_workload(args.config, 0)
+    w = build_workload(args.config, 0, args.batch)
     t = W.device_tensors(w, "cpu" if not torch.cuda.is_available() else "cuda")
     # bounded per-step sample: whole batch when it is cheap, else a prefix of sequences
     max_seqs = 64 if w.name != "long_ctx_70b" else 1
@@ -173,6 +174,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="llama3_8b",
                     choices=["tinyllama_f32", "llama3_8b", "ragged_mha", "long_ctx_70b", "fused_tinyllama"])
+    ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
@@ -199,7 +201,7 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
 
     split = args.config == "long_ctx_70b" and world > 1
-    w = build_workload(args.config, 0 if split else rank)
+    w = build_workload(args.config, 0 if split else rank, args.batch)
     if split:
         s = W.shard_long_context(w, rank, world)
         t = W.device_tensors(s, dev, pool_blocks=s.meta["pool_range"])

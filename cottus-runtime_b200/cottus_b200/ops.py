@@ -62,7 +62,7 @@ def make_decode_params(out, query, kv_pool, block_table, context_lens, *, num_kv
     B, H = query.shape[0], query.shape[1]
     if num_physical_blocks is None:
         per_block = 2 * num_layers * block_size * num_kv_heads * head_dim
-        num_physical_blocks = kv_pool.numel() // per_block
+        num_physical_blocks = kv_pool.numel() // per_block if per_block > 0 else 0
     p = PagedDecodeParams()
     p.out, p.query, p.kv_pool = out.data_ptr(), query.data_ptr(), kv_pool.data_ptr()
     p.block_table, p.context_lens = block_table.data_ptr(), context_lens.data_ptr()

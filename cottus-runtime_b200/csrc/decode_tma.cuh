@@ -62,9 +62,10 @@ struct TmaArgs {
     float qscale;  // softmax scale * log2(e)
 };
 
-// Pages of sequence b, or 0 when its context is empty or invalid.
+// Pages of sequence b, or 0 when its context is empty or invalid; *ctx_out
+// receives the context length.
 template <bool ROPE>
-__device__ __forceinline__ int seq_pages(const TmaArgs& a, int b) {
+__device__ __forceinline__ int seq_pages(const TmaArgs& a, int b, int* ctx_out = nullptr) {
     int n;
     if (ROPE) {
         int pos = a.positions[b];
@@ -73,6 +74,7 @@ __device__ __forceinline__ int seq_pages(const TmaArgs& a, int b) {
     } else {
         n = a.ctx[b];
     }
+    if (ctx_out) *ctx_out = n;
     if (n <= 0 || n > a.maxb * kBS) return 0;
     return (n + kBS - 1) / kBS;
 }
@@ -102,7 +104,7 @@ template <int RING, int D, int G>
 constexpr size_t tma_smem_bytes() {
     using C = TmaCfg<D, G>;
     return (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 8 + (size_t)kNW * C::CH * G * 4 +
-           (size_t)kNW * 2 * G * 4 + 128;
+           (size_t)kNW * 2 * G * 4 + (size_t)kNW * RING * 4 + 128;
 }
 
 // Transpose-reduce: CNT values per lane are summed over the lanes that
@@ -130,7 +132,7 @@ struct TransposeReduce {
 };
 
 struct Cursor {
-    int b, h, p, np;
+    int b, h, p, np, n;  // sequence, kv head, page, pages of b, context of b
 };
 
 template <bool ROPE>
@@ -141,7 +143,7 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const TmaArgs& a) {
             c.h = 0;
             do {
                 ++c.b;
-                c.np = c.b < a.B ? seq_pages<ROPE>(a, c.b) : 1;
+                c.np = c.b < a.B ? seq_pages<ROPE>(a, c.b, &c.n) : 1;
             } while (c.np == 0);
         }
     }
@@ -166,6 +168,9 @@ __global__ void __launch_bounds__(kNW * 32)
     float* hs = reinterpret_cast<float*>(smem + (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 8 +
                                          (size_t)kNW * CH * G * 4) +
                 warp * 2 * G;
+    int* slot_blk = reinterpret_cast<int*>(smem + (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 8 +
+                                           (size_t)kNW * CH * G * 4 + (size_t)kNW * 2 * G * 4) +
+                    warp * RING;
 
     if (lane == 0) {
         if (warp == 0) prefetch_tensormap(&kv_map);
@@ -212,34 +217,38 @@ __global__ void __launch_bounds__(kNW * 32)
             }
             base = __shfl_sync(FULL, incl, 31);
         }
-        const int np = seq_pages<ROPE>(a, found_b);
+        int n_b = 0;
+        const int np = seq_pages<ROPE>(a, found_b, &n_b);
         const long long r = u0 - found_excl;
         cur.b = found_b;
         cur.np = np;
+        cur.n = n_b;
         cur.h = (int)(r / np);
         cur.p = (int)(r % np);
     }
 
-    // ---- TMA issue -------------------------------------------------------
-    auto issue = [&](int k, const Cursor& c) {
+    // ---- TMA issue: lane 0 owns the issue cursor; the block id of the next
+    // unit to issue is loaded one page ahead so its latency hides behind math.
+    Cursor ic = cur;
+    int blk_next = lane == 0 ? a.bt[(long long)ic.b * a.maxb + ic.p] : 0;
+    auto issue = [&](int k) {
         if (lane == 0) {
             const int slot = k % RING;
-            const int blk = a.bt[(long long)c.b * a.maxb + c.p];
+            const int blk = blk_next;
+            slot_blk[slot] = blk;
             if (blk < 0 || (long long)blk >= a.num_blocks) {
                 mbar_arrive(&bars[slot]);  // nothing to load; the consumer masks the page
             } else {
                 mbar_arrive_expect_tx(&bars[slot], C::SLOT_BYTES);
-                tma_load_3d(slots + (size_t)slot * C::SLOT_BYTES, &kv_map, &bars[slot], 0, c.h,
+                tma_load_3d(slots + (size_t)slot * C::SLOT_BYTES, &kv_map, &bars[slot], 0, ic.h,
                             (blk * a.L + a.layer) * (2 * kBS));
             }
+            cursor_next<ROPE>(ic, a);
+            if (k + 1 < nu) blk_next = a.bt[(long long)ic.b * a.maxb + ic.p];
         }
     };
-    Cursor ic = cur;
     const int prime = nu < RING ? nu : RING;
-    for (int k = 0; k < prime; ++k) {
-        issue(k, ic);
-        cursor_next<ROPE>(ic, a);
-    }
+    for (int k = 0; k < prime; ++k) issue(k);
 
     float2 q2[G][4];
     float2 o2[G][4];
@@ -252,7 +261,7 @@ __global__ void __launch_bounds__(kNW * 32)
 
     for (int k = 0; k < nu; ++k) {
         const int slot = k % RING;
-        const int ctx_b = seq_ctx<ROPE>(a, cur.b);
+        const int ctx_b = cur.n;
         if (!seg_open) {
             // ---- segment start: load (and rotate) the group's query rows ----
             seg_open = true;
@@ -288,12 +297,6 @@ __global__ void __launch_bounds__(kNW * 32)
             }
         }
 
-        const int blk = a.bt[(long long)cur.b * a.maxb + cur.p];
-        const bool blk_ok = blk >= 0 && (long long)blk < a.num_blocks;
-        if (!blk_ok && lane == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
-        int n_valid = blk_ok ? ctx_b - cur.p * kBS : 0;
-        n_valid = n_valid > kBS ? kBS : n_valid;
-
         const bool landed = __all_sync(FULL, mbar_wait_bounded(&bars[slot], (k / RING) & 1));
         if (!landed) {
             if (lane == 0) report(a.status, COTTUS_STATUS_TIMEOUT);
@@ -302,6 +305,11 @@ __global__ void __launch_bounds__(kNW * 32)
                 (void)__all_sync(FULL, mbar_wait_bounded(&bars[kk % RING], (kk / RING) & 1));
             return;
         }
+        const int blk = slot_blk[slot];
+        const bool blk_ok = blk >= 0 && (long long)blk < a.num_blocks;
+        if (!blk_ok && lane == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
+        int n_valid = blk_ok ? ctx_b - cur.p * kBS : 0;
+        n_valid = n_valid > kBS ? kBS : n_valid;
         const uint16_t* kt = reinterpret_cast<const uint16_t*>(slots + (size_t)slot * C::SLOT_BYTES);
         const uint16_t* vt = kt + kBS * D;
 
@@ -435,8 +443,7 @@ __global__ void __launch_bounds__(kNW * 32)
         // ---- refill this slot --------------------------------------------
         if (k + RING < nu) {
             fence_proxy_async_smem();
-            issue(k + RING, ic);
-            cursor_next<ROPE>(ic, a);
+            issue(k + RING);
         }
 
         // ---- segment end -------------------------------------------------

@@ -24,8 +24,8 @@ def oracle_outputs(oracle, w, t, seqs, query=None):
 
 
 def torch_reference(w, t, query=None, seqs=None):
-    """fp32 attention on the GPU from a dense torch gather of the pages."""
-    per = w.block_elems()
+    """fp32 attention on the GPU from a dense torch gather of the pages
+    (GQA groups kept as a separate axis, so K/V are not replicated)."""
     pool = t["kv_pool"].view(-1, w.L, 2, w.bs, w.Hkv, w.D)[:, w.layer]
     q = (t["query"] if query is None else query).float()
     G = w.H // w.Hkv
@@ -42,12 +42,10 @@ def torch_reference(w, t, query=None, seqs=None):
         blk = pool.index_select(0, bt[b, :pages])                  # [pages, 2, bs, Hkv, D]
         k = blk[:, 0].reshape(-1, w.Hkv, w.D)[:n].view(torch.float16).float()
         v = blk[:, 1].reshape(-1, w.Hkv, w.D)[:n].view(torch.float16).float()
-        kq = k.repeat_interleave(G, dim=1)                        # [n, H, D]
-        vq = v.repeat_interleave(G, dim=1)
-        s = torch.einsum("hd,nhd->hn", q[b], kq) * scale
+        qg = q[b].view(w.Hkv, G, w.D)
+        s = torch.einsum("kgd,nkd->kgn", qg, k) * scale
         p = torch.softmax(s, dim=-1)
-        outs.append(torch.einsum("hn,nhd->hd", p, vq))
-    _ = per
+        outs.append(torch.einsum("kgn,nkd->kgd", p, v).reshape(w.H, w.D))
     return torch.stack(outs)
 
 
