@@ -51,7 +51,7 @@ def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     key = (device.type, device.index)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
         _WS[key] = buf
     return buf
 

@@ -3,8 +3,8 @@
 // Work decomposition (stream-K over pages): a unit is one 16-token page of
 // one (sequence, kv head) pair; units are ordered sequence-major, then kv
 // head, then page.  Every warp of the persistent grid is a worker that owns
-// an equal contiguous range of units, so skewed (ragged) batches and long
-// contexts balance exactly across the 148 SMs.
+// one contiguous chunk of ceil(units / workers) units (at least kMinChunk),
+// so skewed (ragged) batches and long contexts balance across the 148 SMs.
 //
 // Per warp: a ring of RING shared-memory slots, each holding the K and V
 // tiles (2 x 16 rows x head_dim fp16) of one page for one kv head, filled
@@ -26,7 +26,8 @@
 //
 // A worker writes a finished (sequence, kv head) pair straight to `out`;
 // a pair cut by a worker boundary leaves (m, l, o) partials in the
-// workspace, merged afterwards by split_combine_kernel.
+// workspace; the last worker to finish such a pair (an arrival counter per
+// pair) merges its partials, so one launch does the whole decode.
 //
 // The reference computes the same function per sequence and head with two
 // passes over K (paged_attention_cpu.cpp:53-103); results agree to fp32
@@ -40,6 +41,7 @@ namespace cb200 {
 
 constexpr int kBS = 16;   // tokens per page on the fast path
 constexpr int kNW = 4;    // worker warps per CTA
+constexpr int kMinChunk = 4;  // fewest pages a worker takes (limits partials on tiny batches)
 
 struct TmaArgs {
     void* out;
@@ -50,6 +52,7 @@ struct TmaArgs {
     float* lse;
     float* ws_o;
     float* ws_ml;
+    unsigned long long* counters;  // [B * Hkv] arrival counters of cut pairs, tagged with `epoch`
     uint32_t* status;
     const void* k_new;
     const void* v_new;
@@ -59,7 +62,8 @@ struct TmaArgs {
     long long num_blocks;
     int B, H, Hkv, L, layer, maxb, max_pos;
     int q_f16, out_f16;
-    float qscale;  // softmax scale * log2(e)
+    unsigned epoch;  // per-launch tag of the arrival counters
+    float qscale;    // softmax scale * log2(e)
 };
 
 // Pages of sequence b, or 0 when its context is empty or invalid; *ctx_out
@@ -149,6 +153,90 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const TmaArgs& a) {
     }
 }
 
+// Called by a worker after it stored its partial of a cut (sequence, kv
+// head) pair whose units are [ps, ps + np).  Worker wk owns units
+// [wk*chunk, (wk+1)*chunk), so the pair's partials belong to workers
+// ps/chunk .. (ps+np-1)/chunk, every one of them non-empty.  Arrives on the
+// pair's counter (tagged with the launch epoch, so a count left by an
+// aborted launch reads as zero); the last arriving worker merges all
+// partials (loads spread over the lanes and issued independently) and
+// resets the counter to zero.
+template <int D, int G>
+__device__ __forceinline__ void merge_if_last(const TmaArgs& a, int b, int h, long long ps, int np, long long chunk,
+                                              int lane, int grp, int lq) {
+    constexpr unsigned FULL = 0xffffffffu;
+    constexpr int LW = D / 8, RPS = 32 / LW;
+    const long long w0 = ps / chunk, w1 = (ps + np - 1) / chunk;
+    const int nparts = (int)(w1 - w0 + 1);
+    const long long slot0 = w0 * chunk >= ps ? 2 * w0 : 2 * w0 + 1;  // later parts start inside the pair
+    unsigned long long* ctr = a.counters + (long long)b * a.Hkv + h;
+    int last = 0;
+    __syncwarp();
+    if (lane == 0) {
+        __threadfence();  // this worker's partial is visible before its arrival
+        unsigned long long old = atomicAdd(ctr, 0ull);
+        while (true) {
+            const unsigned long long nv =
+                (unsigned)(old >> 32) == a.epoch ? old + 1 : (((unsigned long long)a.epoch << 32) | 1ull);
+            const unsigned long long prev = atomicCAS(ctr, old, nv);
+            if (prev == old) {
+                last = (int)(nv & 0xffffffffull) == nparts;
+                break;
+            }
+            old = prev;
+        }
+        if (last) __threadfence();
+    }
+    last = __shfl_sync(FULL, last, 0);
+    __syncwarp();
+    if (!last) return;
+    auto slot_of = [&](int j) -> long long { return j == 0 ? slot0 : 2 * (w0 + j); };
+#pragma unroll 1
+    for (int g = 0; g < G; ++g) {
+        // running max and denominator over the parts, one part per lane
+        float M = -INFINITY;
+        for (int j = lane; j < nparts; j += 32) M = fmaxf(M, __ldcg(a.ws_ml + (slot_of(j) * G + g) * 2));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+        float Ls = 0.f;
+        if (M != -INFINITY)
+            for (int j = lane; j < nparts; j += 32) {
+                const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + (slot_of(j) * G + g) * 2));
+                if (ml.x != -INFINITY) Ls += ml.y * exp2f(ml.x - M);
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(FULL, Ls, o);
+        // weighted sum of the outputs: row group r takes parts r, r+RPS, ...
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        if (M != -INFINITY) {
+#pragma unroll 4
+            for (int j = grp; j < nparts; j += RPS) {
+                const long long sl = slot_of(j);
+                const float m = __ldcg(a.ws_ml + (sl * G + g) * 2);
+                const float4* src = reinterpret_cast<const float4*>(a.ws_o + (sl * G + g) * D + lq * 8);
+                const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
+                const float wgt = m == -INFINITY ? 0.f : exp2f(m - M);
+                acc[0] += wgt * x0.x; acc[1] += wgt * x0.y; acc[2] += wgt * x0.z; acc[3] += wgt * x0.w;
+                acc[4] += wgt * x1.x; acc[5] += wgt * x1.y; acc[6] += wgt * x1.z; acc[7] += wgt * x1.w;
+            }
+        }
+#pragma unroll
+        for (int o = LW; o < 32; o <<= 1)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(FULL, acc[i], o);
+        if (grp == 0) {
+            const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] *= inv;
+            const long long head = (long long)b * a.H + (long long)h * G + g;
+            if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + head * D + lq * 8, acc);
+            else store8(reinterpret_cast<float*>(a.out) + head * D + lq * 8, acc);
+            if (a.lse && lq == 0) a.lse[head] = Ls > 0.f ? (M + log2f(Ls)) * kLn2 : -INFINITY;
+        }
+    }
+    if (lane == 0) atomicExch(ctr, 0ull);
+}
+
 template <int D, int G, int RING, bool ROPE>
 __global__ void __launch_bounds__(kNW * 32)
     decode_tma_kernel(const __grid_constant__ CUtensorMap kv_map, const TmaArgs a) {
@@ -188,7 +276,26 @@ __global__ void __launch_bounds__(kNW * 32)
     const long long U = total_pages * a.Hkv;
     const long long W = (long long)gridDim.x * kNW;
     const long long w = (long long)blockIdx.x * kNW + warp;
-    const long long u0 = w * U / W, u1 = (w + 1) * U / W;
+    // equal chunks of at least kMinChunk pages; trailing workers may idle
+    const long long chunk = max((U + W - 1) / W, (long long)kMinChunk);
+    const long long u0 = min(w * chunk, U), u1 = min(u0 + chunk, U);
+
+    // Sequences with no pages (empty or invalid context) get zero rows here;
+    // worker w covers sequences w, w + W, ...
+    for (long long b = w; b < a.B; b += W) {
+        int n = 0;
+        if (seq_pages<ROPE>(a, (int)b, &n) != 0) continue;
+        if (lane == 0 && (ROPE || n != 0))
+            report(a.status, ROPE ? COTTUS_STATUS_BAD_POSITION : COTTUS_STATUS_BAD_CONTEXT);
+        const long long nel = (long long)a.H * D;
+        for (long long i = lane * 8; i < nel; i += 32 * 8) {
+            const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + b * nel + i, z);
+            else store8(reinterpret_cast<float*>(a.out) + b * nel + i, z);
+        }
+        if (a.lse)
+            for (int i = lane; i < a.H; i += 32) a.lse[b * a.H + i] = -INFINITY;
+    }
     if (u0 >= u1) return;
     const int nu = (int)(u1 - u0);
 
@@ -502,96 +609,11 @@ __global__ void __launch_bounds__(kNW * 32)
                     }
                 }
             }
+            if (!whole) merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, grp, lq);
             __syncwarp();
             seg_open = false;
         }
         if (k + 1 < nu) cursor_next<ROPE>(cur, a);
-    }
-}
-
-// Merges the partials of pairs that were cut by worker boundaries, writes
-// zeros for empty/invalid sequences.  One CTA per sequence.
-template <bool ROPE>
-__global__ void __launch_bounds__(256) split_combine_kernel(const TmaArgs a, int G, int D, long long W) {
-    const int b = blockIdx.x;
-    __shared__ long long red[2][8];
-    long long before = 0, total = 0;
-    for (int bb = threadIdx.x; bb < a.B; bb += blockDim.x) {
-        const long long n = seq_pages<ROPE>(a, bb);
-        total += n;
-        if (bb < b) before += n;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        before += __shfl_xor_sync(0xffffffffu, before, o);
-        total += __shfl_xor_sync(0xffffffffu, total, o);
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
-    if (lane == 0) {
-        red[0][warp] = before;
-        red[1][warp] = total;
-    }
-    __syncthreads();
-    before = 0;
-    total = 0;
-    for (int i = 0; i < nwarps; ++i) {
-        before += red[0][i];
-        total += red[1][i];
-    }
-    const int np = seq_pages<ROPE>(a, b);
-    if (np == 0) {
-        const int n = seq_ctx<ROPE>(a, b);
-        if (threadIdx.x == 0 && (n != 0 || ROPE)) report(a.status, ROPE ? COTTUS_STATUS_BAD_POSITION
-                                                                        : COTTUS_STATUS_BAD_CONTEXT);
-        const long long nel = (long long)a.H * D;
-        for (long long i = threadIdx.x; i < nel; i += blockDim.x) {
-            if (a.out_f16) reinterpret_cast<__half*>(a.out)[(long long)b * nel + i] = __float2half_rn(0.f);
-            else reinterpret_cast<float*>(a.out)[(long long)b * nel + i] = 0.f;
-        }
-        if (a.lse)
-            for (int i = threadIdx.x; i < a.H; i += blockDim.x) a.lse[(long long)b * a.H + i] = -INFINITY;
-        return;
-    }
-    const long long U = total * a.Hkv;
-    const long long seq_base = before * a.Hkv;
-    for (int hg = warp; hg < a.Hkv * G; hg += nwarps) {
-        const int h = hg / G, g = hg % G;
-        const long long ps = seq_base + (long long)h * np;
-        const long long pe = ps + np - 1;
-        const long long w0 = ((ps + 1) * W - 1) / U;
-        const long long w1 = ((pe + 1) * W - 1) / U;
-        if (w0 == w1) continue;
-        float M = -INFINITY;
-        for (long long wk = w0; wk <= w1; ++wk) {
-            const long long s0 = wk * U / W, s1 = (wk + 1) * U / W;
-            if (s0 >= s1) continue;
-            const long long slot = s0 >= ps ? 2 * wk : 2 * wk + 1;
-            M = fmaxf(M, a.ws_ml[(slot * G + g) * 2]);
-        }
-        float Ls = 0.f;
-        for (long long wk = w0; wk <= w1; ++wk) {
-            const long long s0 = wk * U / W, s1 = (wk + 1) * U / W;
-            if (s0 >= s1) continue;
-            const long long slot = s0 >= ps ? 2 * wk : 2 * wk + 1;
-            const float m = a.ws_ml[(slot * G + g) * 2];
-            if (m != -INFINITY) Ls += a.ws_ml[(slot * G + g) * 2 + 1] * exp2f(m - M);
-        }
-        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-        const long long head = (long long)b * a.H + (long long)h * G + g;
-        for (int d = lane; d < D; d += 32) {
-            float acc = 0.f;
-            for (long long wk = w0; wk <= w1; ++wk) {
-                const long long s0 = wk * U / W, s1 = (wk + 1) * U / W;
-                if (s0 >= s1) continue;
-                const long long slot = s0 >= ps ? 2 * wk : 2 * wk + 1;
-                const float m = a.ws_ml[(slot * G + g) * 2];
-                if (m != -INFINITY) acc += a.ws_o[(slot * G + g) * D + d] * exp2f(m - M);
-            }
-            acc *= inv;
-            if (a.out_f16) reinterpret_cast<__half*>(a.out)[head * D + d] = __float2half_rn(acc);
-            else reinterpret_cast<float*>(a.out)[head * D + d] = acc;
-        }
-        if (a.lse && lane == 0) a.lse[head] = Ls > 0.f ? (M + log2f(Ls)) * kLn2 : -INFINITY;
     }
 }
 
@@ -600,6 +622,7 @@ __global__ void __launch_bounds__(256) split_combine_kernel(const TmaArgs a, int
 // ---------------------------------------------------------------------------
 CUtensorMap make_kv_tensor_map(const DecodeDesc& d, cudaError_t* err);
 int device_sm_count(int device);
+unsigned next_epoch();
 
 template <int D, int G, int RING, bool ROPE>
 struct TmaLauncher {
@@ -634,8 +657,11 @@ struct TmaLauncher {
         a.ctx = d.context_lens;
         a.positions = d.positions;
         a.lse = d.lse;
-        a.ws_o = reinterpret_cast<float*>(d.workspace);
-        a.ws_ml = reinterpret_cast<float*>(d.workspace) + (size_t)2 * W * G * D;
+        const size_t ctr_bytes = ((size_t)d.batch * d.num_kv_heads * 8 + 255) & ~size_t(255);
+        a.counters = reinterpret_cast<unsigned long long*>(d.workspace);
+        a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(d.workspace) + ctr_bytes);
+        a.ws_ml = a.ws_o + (size_t)2 * W * G * D;
+        a.epoch = next_epoch();
         a.status = d.status;
         a.k_new = d.k_new;
         a.v_new = d.v_new;
@@ -655,9 +681,6 @@ struct TmaLauncher {
         a.qscale = d.scale * kLog2e;
         const size_t smem = tma_smem_bytes<RING, D, G>();
         decode_tma_kernel<D, G, RING, ROPE><<<grid, kNW * 32, smem, st>>>(map, a);
-        err = cudaGetLastError();
-        if (err != cudaSuccess) return err;
-        split_combine_kernel<ROPE><<<d.batch, 256, 0, st>>>(a, G, D, W);
         return cudaGetLastError();
     }
 };

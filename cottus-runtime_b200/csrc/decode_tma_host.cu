@@ -2,6 +2,10 @@
 // KV-pool tensor map, per-device SM count, dispatch by head_dim.
 #include <cudaTypedefs.h>
 
+#include <unistd.h>
+
+#include <atomic>
+#include <chrono>
 #include <cstring>
 #include <mutex>
 
@@ -18,6 +22,21 @@ int device_sm_count(int device) {
         cache[device] = n > 0 ? n : 148;
     }
     return cache[device];
+}
+
+// Launch tags of the pair arrival counters.  Seeded per process so that a
+// counter left behind by an aborted launch of another process is unlikely
+// to carry a live tag; 0 is never used.
+unsigned next_epoch() {
+    static std::atomic<unsigned> ctr{[] {
+        const auto t = (unsigned long long)std::chrono::steady_clock::now().time_since_epoch().count();
+        return (unsigned)((t * 0x9E3779B97F4A7C15ull) >> 32) ^ ((unsigned)getpid() << 16);
+    }()};
+    unsigned e;
+    do {
+        e = ctr.fetch_add(1, std::memory_order_relaxed) + 1;
+    } while (e == 0);
+    return e;
 }
 
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -90,7 +109,8 @@ static size_t workers(const DecodeDesc& d) {
 size_t tma_workspace_bytes(const DecodeDesc& d) {
     const size_t W = workers(d);
     const size_t G = (size_t)(d.num_heads / d.num_kv_heads);
-    return 2 * W * G * ((size_t)d.head_dim + 2) * sizeof(float) + 256;
+    const size_t ctr_bytes = ((size_t)d.batch * d.num_kv_heads * 8 + 255) & ~size_t(255);
+    return ctr_bytes + 2 * W * G * ((size_t)d.head_dim + 2) * sizeof(float) + 256;
 }
 
 cudaError_t launch_decode_tma(const DecodeDesc& d, cudaStream_t st) {
