@@ -153,6 +153,65 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const TmaArgs& a) {
     }
 }
 
+// Sequences with no pages (empty or invalid context) get zero output rows;
+// worker w covers sequences w, w + W, ...
+template <int D, bool ROPE>
+__device__ __forceinline__ void zero_empty_sequences(const TmaArgs& a, long long w, long long W, int lane) {
+    for (long long b = w; b < a.B; b += W) {
+        int n = 0;
+        if (seq_pages<ROPE>(a, (int)b, &n) != 0) continue;
+        if (lane == 0 && (ROPE || n != 0))
+            report(a.status, ROPE ? COTTUS_STATUS_BAD_POSITION : COTTUS_STATUS_BAD_CONTEXT);
+        const long long nel = (long long)a.H * D;
+        for (long long i = lane * 8; i < nel; i += 32 * 8) {
+            const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + b * nel + i, z);
+            else store8(reinterpret_cast<float*>(a.out) + b * nel + i, z);
+        }
+        if (a.lse)
+            for (int i = lane; i < a.H; i += 32) a.lse[b * a.H + i] = -INFINITY;
+    }
+}
+
+// (sequence, kv head, page) of unit u (< total units): a warp-wide prefix
+// scan over the sequences' page counts, then division by the page count.
+template <bool ROPE>
+__device__ __forceinline__ Cursor locate_unit(const TmaArgs& a, long long u, int lane) {
+    constexpr unsigned FULL = 0xffffffffu;
+    long long base = 0;
+    int found_b = -1;
+    long long found_excl = 0;
+    for (int bb = 0; bb < a.B && found_b < 0; bb += 32) {
+        const int b = bb + lane;
+        const long long units = b < a.B ? (long long)seq_pages<ROPE>(a, b) * a.Hkv : 0;
+        long long incl = units;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            long long t = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += t;
+        }
+        incl += base;
+        const long long excl = incl - units;
+        const unsigned hit = __ballot_sync(FULL, units > 0 && excl <= u && u < incl);
+        if (hit) {
+            const int src = __ffs(hit) - 1;
+            found_b = bb + src;
+            found_excl = __shfl_sync(FULL, excl, src);
+        }
+        base = __shfl_sync(FULL, incl, 31);
+    }
+    Cursor c;
+    int n_b = 0;
+    const int np = seq_pages<ROPE>(a, found_b, &n_b);
+    const long long r = u - found_excl;
+    c.b = found_b;
+    c.np = np;
+    c.n = n_b;
+    c.h = (int)(r / np);
+    c.p = (int)(r % np);
+    return c;
+}
+
 // Called by a worker after it stored its partial of a cut (sequence, kv
 // head) pair whose units are [ps, ps + np).  Worker wk owns units
 // [wk*chunk, (wk+1)*chunk), so the pair's partials belong to workers
@@ -280,59 +339,11 @@ __global__ void __launch_bounds__(kNW * 32)
     const long long chunk = max((U + W - 1) / W, (long long)kMinChunk);
     const long long u0 = min(w * chunk, U), u1 = min(u0 + chunk, U);
 
-    // Sequences with no pages (empty or invalid context) get zero rows here;
-    // worker w covers sequences w, w + W, ...
-    for (long long b = w; b < a.B; b += W) {
-        int n = 0;
-        if (seq_pages<ROPE>(a, (int)b, &n) != 0) continue;
-        if (lane == 0 && (ROPE || n != 0))
-            report(a.status, ROPE ? COTTUS_STATUS_BAD_POSITION : COTTUS_STATUS_BAD_CONTEXT);
-        const long long nel = (long long)a.H * D;
-        for (long long i = lane * 8; i < nel; i += 32 * 8) {
-            const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + b * nel + i, z);
-            else store8(reinterpret_cast<float*>(a.out) + b * nel + i, z);
-        }
-        if (a.lse)
-            for (int i = lane; i < a.H; i += 32) a.lse[b * a.H + i] = -INFINITY;
-    }
+    zero_empty_sequences<D, ROPE>(a, w, W, lane);
     if (u0 >= u1) return;
     const int nu = (int)(u1 - u0);
 
-    // locate u0: sequence by warp-wide prefix scan, then kv head and page
-    Cursor cur;
-    {
-        long long base = 0;
-        int found_b = -1;
-        long long found_excl = 0;
-        for (int bb = 0; bb < a.B && found_b < 0; bb += 32) {
-            const int b = bb + lane;
-            const long long units = b < a.B ? (long long)seq_pages<ROPE>(a, b) * a.Hkv : 0;
-            long long incl = units;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                long long t = __shfl_up_sync(FULL, incl, o);
-                if (lane >= o) incl += t;
-            }
-            incl += base;
-            const long long excl = incl - units;
-            const unsigned hit = __ballot_sync(FULL, units > 0 && excl <= u0 && u0 < incl);
-            if (hit) {
-                const int src = __ffs(hit) - 1;
-                found_b = bb + src;
-                found_excl = __shfl_sync(FULL, excl, src);
-            }
-            base = __shfl_sync(FULL, incl, 31);
-        }
-        int n_b = 0;
-        const int np = seq_pages<ROPE>(a, found_b, &n_b);
-        const long long r = u0 - found_excl;
-        cur.b = found_b;
-        cur.np = np;
-        cur.n = n_b;
-        cur.h = (int)(r / np);
-        cur.p = (int)(r % np);
-    }
+    Cursor cur = locate_unit<ROPE>(a, u0, lane);
 
     // ---- TMA issue: lane 0 owns the issue cursor; the block id of the next
     // unit to issue is loaded one page ahead so its latency hides behind math.
@@ -620,9 +631,44 @@ __global__ void __launch_bounds__(kNW * 32)
 // ---------------------------------------------------------------------------
 // Host side of one head_dim: tensor map, occupancy cache, launch.
 // ---------------------------------------------------------------------------
-CUtensorMap make_kv_tensor_map(const DecodeDesc& d, cudaError_t* err);
+CUtensorMap make_kv_tensor_map(const DecodeDesc& d, bool swizzle128, cudaError_t* err);
 int device_sm_count(int device);
 unsigned next_epoch();
+
+// Kernel arguments of one launch; the workspace holds the pair counters,
+// then 2*W partial slots of G x D outputs and G x (m, l).
+inline TmaArgs make_tma_args(const DecodeDesc& d, long long W, int G, int D) {
+    TmaArgs a;
+    a.out = d.out;
+    a.q = d.q;
+    a.bt = d.block_table;
+    a.ctx = d.context_lens;
+    a.positions = d.positions;
+    a.lse = d.lse;
+    const size_t ctr_bytes = ((size_t)d.batch * d.num_kv_heads * 8 + 255) & ~size_t(255);
+    a.counters = reinterpret_cast<unsigned long long*>(d.workspace);
+    a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(d.workspace) + ctr_bytes);
+    a.ws_ml = a.ws_o + (size_t)2 * W * G * D;
+    a.status = d.status;
+    a.k_new = d.k_new;
+    a.v_new = d.v_new;
+    a.cos_sin = d.cos_sin;
+    a.q_out = d.q_out;
+    a.kv = d.kv_mut;
+    a.num_blocks = d.num_blocks;
+    a.B = d.batch;
+    a.H = d.num_heads;
+    a.Hkv = d.num_kv_heads;
+    a.L = d.num_layers;
+    a.layer = d.layer;
+    a.maxb = d.max_blocks;
+    a.max_pos = d.max_position;
+    a.q_f16 = d.q_f16;
+    a.out_f16 = d.out_f16;
+    a.epoch = next_epoch();
+    a.qscale = d.scale * kLog2e;
+    return a;
+}
 
 template <int D, int G, int RING, bool ROPE>
 struct TmaLauncher {
@@ -648,37 +694,9 @@ struct TmaLauncher {
         const long long W = workers(dev);
         const int grid = (int)(W / kNW);
         cudaError_t err = cudaSuccess;
-        const CUtensorMap map = make_kv_tensor_map(d, &err);
+        const CUtensorMap map = make_kv_tensor_map(d, false, &err);
         if (err != cudaSuccess) return err;
-        TmaArgs a;
-        a.out = d.out;
-        a.q = d.q;
-        a.bt = d.block_table;
-        a.ctx = d.context_lens;
-        a.positions = d.positions;
-        a.lse = d.lse;
-        const size_t ctr_bytes = ((size_t)d.batch * d.num_kv_heads * 8 + 255) & ~size_t(255);
-        a.counters = reinterpret_cast<unsigned long long*>(d.workspace);
-        a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(d.workspace) + ctr_bytes);
-        a.ws_ml = a.ws_o + (size_t)2 * W * G * D;
-        a.epoch = next_epoch();
-        a.status = d.status;
-        a.k_new = d.k_new;
-        a.v_new = d.v_new;
-        a.cos_sin = d.cos_sin;
-        a.q_out = d.q_out;
-        a.kv = d.kv_mut;
-        a.num_blocks = d.num_blocks;
-        a.B = d.batch;
-        a.H = d.num_heads;
-        a.Hkv = d.num_kv_heads;
-        a.L = d.num_layers;
-        a.layer = d.layer;
-        a.maxb = d.max_blocks;
-        a.max_pos = d.max_position;
-        a.q_f16 = d.q_f16;
-        a.out_f16 = d.out_f16;
-        a.qscale = d.scale * kLog2e;
+        TmaArgs a = make_tma_args(d, W, G, D);
         const size_t smem = tma_smem_bytes<RING, D, G>();
         decode_tma_kernel<D, G, RING, ROPE><<<grid, kNW * 32, smem, st>>>(map, a);
         return cudaGetLastError();

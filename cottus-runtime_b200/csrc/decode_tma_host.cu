@@ -58,7 +58,7 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 //   dim2 = (block, layer, K|V, token) rows (stride num_kv_heads*head_dim).
 // One 16 x 2 box row range of dim2 covers the K rows then the V rows of a
 // page/layer, so box {head_dim, 1, 32} loads both tiles of one kv head.
-CUtensorMap make_kv_tensor_map(const DecodeDesc& d, cudaError_t* err) {
+CUtensorMap make_kv_tensor_map(const DecodeDesc& d, bool swizzle128, cudaError_t* err) {
     CUtensorMap map;
     std::memset(&map, 0, sizeof map);
     auto fn = encode_fn();
@@ -70,10 +70,13 @@ CUtensorMap make_kv_tensor_map(const DecodeDesc& d, cudaError_t* err) {
     cuuint64_t dims[3] = {(cuuint64_t)d.head_dim, (cuuint64_t)d.num_kv_heads,
                           (cuuint64_t)d.num_blocks * d.num_layers * 2 * kBS};
     cuuint64_t strides[2] = {(cuuint64_t)d.head_dim * 2, (cuuint64_t)d.num_kv_heads * d.head_dim * 2};
-    cuuint32_t box[3] = {(cuuint32_t)d.head_dim, 1, 2 * kBS};
+    // plain: one {head_dim, 1, 32} box per page; swizzled: {64, 1, 32} boxes
+    // (128-byte rows, 128B swizzle) for conflict-free ldmatrix
+    cuuint32_t box[3] = {swizzle128 ? 64u : (cuuint32_t)d.head_dim, 1, 2 * kBS};
     cuuint32_t estr[3] = {1, 1, 1};
     CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     *err = r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
     return map;
@@ -97,7 +100,16 @@ bool tma_supported(const DecodeDesc& d) {
     return true;
 }
 
+bool mma_supported(const DecodeDesc& d) {
+    if (!tma_supported(d)) return false;
+    if (d.head_dim != 64 && d.head_dim != 128) return false;
+    // fp16 probabilities: only where the result is fp16, or fp32 LSE
+    // partials whose merge is (split contexts)
+    return d.out_f16 || d.lse != nullptr;
+}
+
 static size_t workers(const DecodeDesc& d) {
+    if (mma_supported(d)) return d.head_dim == 64 ? mma_workers_d64(d) : mma_workers_d128(d);
     switch (d.head_dim) {
         case 64: return tma_workers_d64(d);
         case 128: return tma_workers_d128(d);
@@ -114,6 +126,7 @@ size_t tma_workspace_bytes(const DecodeDesc& d) {
 }
 
 cudaError_t launch_decode_tma(const DecodeDesc& d, cudaStream_t st) {
+    if (mma_supported(d)) return d.head_dim == 64 ? launch_decode_mma_d64(d, st) : launch_decode_mma_d128(d, st);
     switch (d.head_dim) {
         case 64: return launch_decode_tma_d64(d, st);
         case 128: return launch_decode_tma_d128(d, st);

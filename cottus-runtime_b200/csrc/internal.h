@@ -50,6 +50,14 @@ size_t tma_workers_d64(const DecodeDesc& d);
 size_t tma_workers_d128(const DecodeDesc& d);
 size_t tma_workers_d256(const DecodeDesc& d);
 
+// Tensor-core variant of the fast path (head_dim 64/128, fp16 output or
+// LSE partials).
+bool mma_supported(const DecodeDesc& d);
+cudaError_t launch_decode_mma_d64(const DecodeDesc& d, cudaStream_t st);
+cudaError_t launch_decode_mma_d128(const DecodeDesc& d, cudaStream_t st);
+size_t mma_workers_d64(const DecodeDesc& d);
+size_t mma_workers_d128(const DecodeDesc& d);
+
 // Generic path: any head_dim <= 512, any block size; one CTA per (seq, head).
 cudaError_t launch_decode_generic(const DecodeDesc& d, cudaStream_t st);
 

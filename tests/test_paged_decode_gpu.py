@@ -199,12 +199,18 @@ def test_max_context_and_single_sequence(oracle):
     assert max_abs(run(w, t), oracle_outputs(oracle, w, t, [0])) <= TOL_F32
 
 
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
 @pytest.mark.parametrize("G", [1, 2, 4, 8])
 @pytest.mark.parametrize("D", [64, 128, 256])
-def test_group_and_head_dim_grid(oracle, G, D):
-    w = _custom([5, 77, 300], H=2 * G, Hkv=2, D=D, seed=G * 1000 + D)
+def test_group_and_head_dim_grid(oracle, G, D, out_dtype):
+    """Every (group, head_dim) instantiation: fp32 outputs use the SIMT
+    kernel, fp16 outputs the tensor-core kernel (head_dim 64/128)."""
+    w = _custom([5, 77, 300, 16], H=2 * G, Hkv=2, D=D, seed=G * 1000 + D)
     t = W.device_tensors(w, DEV)
-    assert max_abs(run(w, t), oracle_outputs(oracle, w, t, range(w.B))) <= TOL_F32
+    got = run(w, t, out_dtype=out_dtype)
+    assert max_abs(got, oracle_outputs(oracle, w, t, range(w.B))) <= tol_for(out_dtype)
+    t32 = dict(t, query=t["query"].float())  # fp32 queries: split into fp16 hi/lo on the tensor-core path
+    assert max_abs(run(w, t32, out_dtype=out_dtype), oracle_outputs(oracle, w, t32, range(w.B))) <= tol_for(out_dtype)
 
 
 @pytest.mark.parametrize("H,Hkv,D,bs", [(6, 4, 64, 16), (4, 4, 40, 16), (16, 2, 128, 32), (2, 1, 96, 7)])
