@@ -169,6 +169,12 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Programmatic dependent launch: wait until the preceding kernel of the
+// stream has completed (and its writes are visible) before touching global
+// memory; let the next kernel of the stream start its own prologue early.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void report(uint32_t* status, uint32_t bits) {
     if (status) atomicOr(status, bits);
 }

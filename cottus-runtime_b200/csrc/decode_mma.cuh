@@ -93,19 +93,16 @@ __global__ void __launch_bounds__(kNW * 32)
     }
     __syncwarp();
 
-    long long total_pages = 0;
-    for (int b = lane; b < a.B; b += 32) total_pages += seq_pages<ROPE>(a, b);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) total_pages += __shfl_xor_sync(FULL, total_pages, o);
-    const long long U = total_pages * a.Hkv;
+    grid_dependency_wait();
+    grid_dependents_launch();
+
     const long long W = (long long)gridDim.x * kNW;
     const long long w = (long long)blockIdx.x * kNW + warp;
-    const long long chunk = max((U + W - 1) / W, (long long)kMinChunk);
-    const long long u0 = min(w * chunk, U), u1 = min(u0 + chunk, U);
-    zero_empty_sequences<D, ROPE>(a, w, W, lane);
+    const WorkerPlan pl = plan_worker<D, ROPE>(a, w, W, lane);
+    const long long chunk = pl.chunk, u0 = pl.u0, u1 = pl.u1;
     if (u0 >= u1) return;
     const int nu = (int)(u1 - u0);
-    Cursor cur = locate_unit<ROPE>(a, u0, lane);
+    Cursor cur = pl.cur;
 
     // ---- TMA issue (lane 0), block id prefetched one page ahead ----------
     Cursor ic = cur;
@@ -141,14 +138,38 @@ __global__ void __launch_bounds__(kNW * 32)
     uint32_t qb[KS][2];
     uint32_t ql[QSPLIT ? KS : 1][2];
     float o[KS][4];
+    float qs[KS][4];  // raw query values of the next segment (loaded a page early)
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     bool seg_open = false, seg_first = true;
     int seg_start_p = 0;
+
+    // this lane's query elements of pair (b, h): head qr, dims kk*16 + 2qc + {0, 1, 8, 9}
+    auto load_q = [&](int b, int h) {
+        const bool live = qr < G;
+        const long long qrow = ((long long)b * a.H + (long long)h * G + (live ? qr : 0)) * D;
+#pragma unroll
+        for (int kk = 0; kk < KS; ++kk) {
+            const int d0 = kk * 16 + 2 * qc, d1 = d0 + 8;
+            float2 u = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
+            if (live) {
+                if (a.q_f16) {
+                    u = unpack_h2(__ldg(reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow + d0)));
+                    v = unpack_h2(__ldg(reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow + d1)));
+                } else {
+                    u = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d0));
+                    v = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d1));
+                }
+            }
+            qs[kk][0] = u.x; qs[kk][1] = u.y; qs[kk][2] = v.x; qs[kk][3] = v.y;
+        }
+    };
+    load_q(cur.b, cur.h);
 
     for (int k = 0; k < nu; ++k) {
         const int slot = k % RING;
         const int ctx_b = cur.n;
         if (!seg_open) {
+            // ---- segment start: (rotate,) split and pack the staged query ----
             seg_open = true;
             seg_first = (k == 0);
             seg_start_p = cur.p;
@@ -159,20 +180,7 @@ __global__ void __launch_bounds__(kNW * 32)
 #pragma unroll
             for (int kk = 0; kk < KS; ++kk) {
                 const int d0 = kk * 16 + 2 * qc, d1 = d0 + 8;
-                float x[4] = {0.f, 0.f, 0.f, 0.f};
-                if (live) {
-                    if (a.q_f16) {
-                        const float2 u = unpack_h2(*reinterpret_cast<const uint32_t*>(
-                            reinterpret_cast<const __half*>(a.q) + qrow + d0));
-                        const float2 v = unpack_h2(*reinterpret_cast<const uint32_t*>(
-                            reinterpret_cast<const __half*>(a.q) + qrow + d1));
-                        x[0] = u.x; x[1] = u.y; x[2] = v.x; x[3] = v.y;
-                    } else {
-                        const float2 u = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d0);
-                        const float2 v = *reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d1);
-                        x[0] = u.x; x[1] = u.y; x[2] = v.x; x[3] = v.y;
-                    }
-                }
+                float x[4] = {qs[kk][0], qs[kk][1], qs[kk][2], qs[kk][3]};
                 if (ROPE && live) {
                     const float* cs = a.cos_sin + (long long)(ctx_b - 1) * D;  // row of D/2 (cos, sin) pairs
                     const float2 c0 = *reinterpret_cast<const float2*>(cs + d0);
@@ -199,6 +207,13 @@ __global__ void __launch_bounds__(kNW * 32)
 #pragma unroll
                 for (int i = 0; i < 4; ++i) o[kk][i] = 0.f;
             }
+        }
+        if (cur.p == cur.np - 1 && k + 1 < nu) {
+            // this page ends the segment: stage the next pair's query now so
+            // the load latency hides behind this page's math
+            Cursor nx = cur;
+            cursor_next<ROPE>(nx, a);
+            load_q(nx.b, nx.h);
         }
 
         const bool landed = __all_sync(FULL, mbar_wait_bounded(&bars[slot], (k / RING) & 1));
@@ -408,8 +423,8 @@ struct MmaLauncher {
         const CUtensorMap map = make_kv_tensor_map(d, true, &err);
         if (err != cudaSuccess) return err;
         TmaArgs a = make_tma_args(d, W, G, D);
-        decode_mma_kernel<D, G, RING, ROPE, QSPLIT><<<(int)(W / kNW), kNW * 32, mma_smem_bytes<RING, D>(), st>>>(map, a);
-        return cudaGetLastError();
+        return launch_pdl(decode_mma_kernel<D, G, RING, ROPE, QSPLIT>, (int)(W / kNW), mma_smem_bytes<RING, D>(), st,
+                          map, a);
     }
 };
 

@@ -1,8 +1,8 @@
-// Tensor-core path instantiations for head_dim 128 (ring of 3 pages per warp).
+// Tensor-core path instantiations for head_dim 128 (ring of 2 pages per warp).
 #include "decode_mma.cuh"
 
 #ifndef CB200_MMA_RING_D128
-#define CB200_MMA_RING_D128 3
+#define CB200_MMA_RING_D128 2
 #endif
 
 namespace cb200 {

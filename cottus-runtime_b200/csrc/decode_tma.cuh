@@ -41,7 +41,7 @@ namespace cb200 {
 
 constexpr int kBS = 16;   // tokens per page on the fast path
 constexpr int kNW = 4;    // worker warps per CTA
-constexpr int kMinChunk = 4;  // fewest pages a worker takes (limits partials on tiny batches)
+constexpr int kMinChunk = 8;  // fewest pages a worker takes (limits partials on tiny batches)
 
 struct TmaArgs {
     void* out;
@@ -212,6 +212,107 @@ __device__ __forceinline__ Cursor locate_unit(const TmaArgs& a, long long u, int
     return c;
 }
 
+// This worker's share of the launch: total units U, chunk size, its unit
+// range [u0, u1) and the cursor at u0.  For batches up to kPlanRegs*32
+// sequences the page counts are loaded once into registers and both the
+// total and the start position come from them; larger batches fall back to
+// repeated scans.  Also zero-fills the outputs of sequences without pages.
+constexpr int kPlanRegs = 8;
+struct WorkerPlan {
+    long long U, chunk, u0, u1;
+    Cursor cur;
+};
+
+template <int D, bool ROPE>
+__device__ __forceinline__ WorkerPlan plan_worker(const TmaArgs& a, long long w, long long W, int lane) {
+    constexpr unsigned FULL = 0xffffffffu;
+    WorkerPlan pl;
+    if (a.B > 32 * kPlanRegs) {
+        long long total_pages = 0;
+        for (int b = lane; b < a.B; b += 32) total_pages += seq_pages<ROPE>(a, b);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) total_pages += __shfl_xor_sync(FULL, total_pages, o);
+        pl.U = total_pages * a.Hkv;
+        pl.chunk = max((pl.U + W - 1) / W, (long long)kMinChunk);
+        pl.u0 = min(w * pl.chunk, pl.U);
+        pl.u1 = min(pl.u0 + pl.chunk, pl.U);
+        zero_empty_sequences<D, ROPE>(a, w, W, lane);
+        if (pl.u0 < pl.u1) pl.cur = locate_unit<ROPE>(a, pl.u0, lane);
+        return pl;
+    }
+    int pg[kPlanRegs], cx[kPlanRegs];
+    long long total = 0;
+#pragma unroll
+    for (int i = 0; i < kPlanRegs; ++i) {
+        const int b = lane + 32 * i;
+        cx[i] = 0;
+        pg[i] = b < a.B ? seq_pages<ROPE>(a, b, &cx[i]) : 0;
+        total += pg[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(FULL, total, o);
+    pl.U = total * a.Hkv;
+    pl.chunk = max((pl.U + W - 1) / W, (long long)kMinChunk);
+    pl.u0 = min(w * pl.chunk, pl.U);
+    pl.u1 = min(pl.u0 + pl.chunk, pl.U);
+    // worker i < kPlanRegs zero-fills the empty sequences among 32i .. 32i+31
+#pragma unroll
+    for (int i = 0; i < kPlanRegs; ++i) {
+        if (w != i) continue;
+        const int b = lane + 32 * i;
+        unsigned empty = __ballot_sync(FULL, b < a.B && pg[i] == 0);
+        if (b < a.B && pg[i] == 0 && (ROPE || cx[i] != 0))
+            report(a.status, ROPE ? COTTUS_STATUS_BAD_POSITION : COTTUS_STATUS_BAD_CONTEXT);
+        const long long nel = (long long)a.H * D;
+        while (empty) {
+            const int src = __ffs(empty) - 1;
+            empty &= empty - 1;
+            const long long bb = 32 * i + src;
+            const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (long long e = lane * 8; e < nel; e += 32 * 8) {
+                if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + bb * nel + e, z);
+                else store8(reinterpret_cast<float*>(a.out) + bb * nel + e, z);
+            }
+            if (a.lse)
+                for (int e = lane; e < a.H; e += 32) a.lse[bb * a.H + e] = -INFINITY;
+        }
+    }
+    if (pl.u0 >= pl.u1) return pl;
+    // locate u0 from the cached page counts
+    long long base = 0;
+    int fb = -1, fnp = 0, fn = 0;
+    long long fex = 0;
+#pragma unroll
+    for (int i = 0; i < kPlanRegs; ++i) {
+        if (fb >= 0) break;
+        const long long units = (long long)pg[i] * a.Hkv;
+        long long incl = units;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long t = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += t;
+        }
+        incl += base;
+        const long long excl = incl - units;
+        const unsigned hit = __ballot_sync(FULL, units > 0 && excl <= pl.u0 && pl.u0 < incl);
+        if (hit) {
+            const int src = __ffs(hit) - 1;
+            fb = 32 * i + src;
+            fex = __shfl_sync(FULL, excl, src);
+            fnp = __shfl_sync(FULL, pg[i], src);
+            fn = __shfl_sync(FULL, cx[i], src);
+        }
+        base = __shfl_sync(FULL, incl, 31);
+    }
+    const long long r = pl.u0 - fex;
+    pl.cur.b = fb;
+    pl.cur.np = fnp;
+    pl.cur.n = fn;
+    pl.cur.h = (int)(r / fnp);
+    pl.cur.p = (int)(r % fnp);
+    return pl;
+}
+
 // Called by a worker after it stored its partial of a cut (sequence, kv
 // head) pair whose units are [ps, ps + np).  Worker wk owns units
 // [wk*chunk, (wk+1)*chunk), so the pair's partials belong to workers
@@ -224,7 +325,8 @@ template <int D, int G>
 __device__ __forceinline__ void merge_if_last(const TmaArgs& a, int b, int h, long long ps, int np, long long chunk,
                                               int lane, int grp, int lq) {
     constexpr unsigned FULL = 0xffffffffu;
-    constexpr int LW = D / 8, RPS = 32 / LW;
+    (void)grp;
+    (void)lq;
     const long long w0 = ps / chunk, w1 = (ps + np - 1) / chunk;
     const int nparts = (int)(w1 - w0 + 1);
     const long long slot0 = w0 * chunk >= ps ? 2 * w0 : 2 * w0 + 1;  // later parts start inside the pair
@@ -250,48 +352,61 @@ __device__ __forceinline__ void merge_if_last(const TmaArgs& a, int b, int h, lo
     __syncwarp();
     if (!last) return;
     auto slot_of = [&](int j) -> long long { return j == 0 ? slot0 : 2 * (w0 + j); };
-#pragma unroll 1
+    // (1) per head: max and rescaled denominator over the parts.  Items
+    // (part j, head g) are spread over the lanes; lanes congruent mod G hold
+    // the same head, so a butterfly over the higher lane bits reduces them.
+    float M = -INFINITY, Ls = 0.f;
+    const int gi = lane % G;
+    for (int i = lane; i < nparts * G; i += 32)
+        M = fmaxf(M, __ldcg(a.ws_ml + (slot_of(i / G) * G + gi) * 2));
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
+    for (int i = lane; i < nparts * G; i += 32) {
+        const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + (slot_of(i / G) * G + gi) * 2));
+        if (ml.x != -INFINITY) Ls += ml.y * exp2f(ml.x - M);
+    }
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1) Ls += __shfl_xor_sync(FULL, Ls, o);
+    // every lane learns (M, Ls) of every head from lanes 0..G-1
+    float Mh[G], Lh[G];
+#pragma unroll
     for (int g = 0; g < G; ++g) {
-        // running max and denominator over the parts, one part per lane
-        float M = -INFINITY;
-        for (int j = lane; j < nparts; j += 32) M = fmaxf(M, __ldcg(a.ws_ml + (slot_of(j) * G + g) * 2));
+        Mh[g] = __shfl_sync(FULL, M, g);
+        Lh[g] = __shfl_sync(FULL, Ls, g);
+    }
+    // (2) outputs: items (head g, 8-dim chunk c) spread over the lanes; each
+    // lane sums its items over the parts with independent loads.
+    constexpr int CPR = D / 8;  // chunks per head row
+#pragma unroll 1
+    for (int it = lane; it < G * CPR; it += 32) {
+        const int g = it / CPR, c = it % CPR;
+        float Mg = Mh[0], Lg = Lh[0];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
-        float Ls = 0.f;
-        if (M != -INFINITY)
-            for (int j = lane; j < nparts; j += 32) {
-                const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + (slot_of(j) * G + g) * 2));
-                if (ml.x != -INFINITY) Ls += ml.y * exp2f(ml.x - M);
+        for (int gg = 1; gg < G; ++gg)
+            if (g == gg) {
+                Mg = Mh[gg];
+                Lg = Lh[gg];
             }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) Ls += __shfl_xor_sync(FULL, Ls, o);
-        // weighted sum of the outputs: row group r takes parts r, r+RPS, ...
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (M != -INFINITY) {
+        if (Mg != -INFINITY) {
 #pragma unroll 4
-            for (int j = grp; j < nparts; j += RPS) {
+            for (int j = 0; j < nparts; ++j) {
                 const long long sl = slot_of(j);
                 const float m = __ldcg(a.ws_ml + (sl * G + g) * 2);
-                const float4* src = reinterpret_cast<const float4*>(a.ws_o + (sl * G + g) * D + lq * 8);
+                const float4* src = reinterpret_cast<const float4*>(a.ws_o + (sl * G + g) * D + c * 8);
                 const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
-                const float wgt = m == -INFINITY ? 0.f : exp2f(m - M);
+                const float wgt = m == -INFINITY ? 0.f : exp2f(m - Mg);
                 acc[0] += wgt * x0.x; acc[1] += wgt * x0.y; acc[2] += wgt * x0.z; acc[3] += wgt * x0.w;
                 acc[4] += wgt * x1.x; acc[5] += wgt * x1.y; acc[6] += wgt * x1.z; acc[7] += wgt * x1.w;
             }
         }
+        const float inv = Lg > 0.f ? 1.f / Lg : 0.f;
 #pragma unroll
-        for (int o = LW; o < 32; o <<= 1)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] += __shfl_xor_sync(FULL, acc[i], o);
-        if (grp == 0) {
-            const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] *= inv;
-            const long long head = (long long)b * a.H + (long long)h * G + g;
-            if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + head * D + lq * 8, acc);
-            else store8(reinterpret_cast<float*>(a.out) + head * D + lq * 8, acc);
-            if (a.lse && lq == 0) a.lse[head] = Ls > 0.f ? (M + log2f(Ls)) * kLn2 : -INFINITY;
-        }
+        for (int i = 0; i < 8; ++i) acc[i] *= inv;
+        const long long head = (long long)b * a.H + (long long)h * G + g;
+        if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + head * D + c * 8, acc);
+        else store8(reinterpret_cast<float*>(a.out) + head * D + c * 8, acc);
+        if (a.lse && c == 0) a.lse[head] = Lg > 0.f ? (Mg + log2f(Lg)) * kLn2 : -INFINITY;
     }
     if (lane == 0) atomicExch(ctr, 0ull);
 }
@@ -327,23 +442,17 @@ __global__ void __launch_bounds__(kNW * 32)
     }
     __syncwarp();
 
+    grid_dependency_wait();
+    grid_dependents_launch();
+
     // ---- this worker's unit range --------------------------------------
-    long long total_pages = 0;
-    for (int b = lane; b < a.B; b += 32) total_pages += seq_pages<ROPE>(a, b);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) total_pages += __shfl_xor_sync(FULL, total_pages, o);
-    const long long U = total_pages * a.Hkv;
     const long long W = (long long)gridDim.x * kNW;
     const long long w = (long long)blockIdx.x * kNW + warp;
-    // equal chunks of at least kMinChunk pages; trailing workers may idle
-    const long long chunk = max((U + W - 1) / W, (long long)kMinChunk);
-    const long long u0 = min(w * chunk, U), u1 = min(u0 + chunk, U);
-
-    zero_empty_sequences<D, ROPE>(a, w, W, lane);
+    const WorkerPlan pl = plan_worker<D, ROPE>(a, w, W, lane);
+    const long long chunk = pl.chunk, u0 = pl.u0, u1 = pl.u1;
     if (u0 >= u1) return;
     const int nu = (int)(u1 - u0);
-
-    Cursor cur = locate_unit<ROPE>(a, u0, lane);
+    Cursor cur = pl.cur;
 
     // ---- TMA issue: lane 0 owns the issue cursor; the block id of the next
     // unit to issue is loaded one page ahead so its latency hides behind math.
@@ -635,6 +744,25 @@ CUtensorMap make_kv_tensor_map(const DecodeDesc& d, bool swizzle128, cudaError_t
 int device_sm_count(int device);
 unsigned next_epoch();
 
+// Launch with programmatic stream serialization: the kernel may begin its
+// prologue while the previous kernel of the stream drains; it waits
+// (griddepcontrol.wait) before reading any global memory.
+template <typename Kern>
+inline cudaError_t launch_pdl(Kern kern, int grid, size_t smem, cudaStream_t st, const CUtensorMap& map,
+                              const TmaArgs& a) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kNW * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, map, a);
+}
+
 // Kernel arguments of one launch; the workspace holds the pair counters,
 // then 2*W partial slots of G x D outputs and G x (m, l).
 inline TmaArgs make_tma_args(const DecodeDesc& d, long long W, int G, int D) {
@@ -697,9 +825,7 @@ struct TmaLauncher {
         const CUtensorMap map = make_kv_tensor_map(d, false, &err);
         if (err != cudaSuccess) return err;
         TmaArgs a = make_tma_args(d, W, G, D);
-        const size_t smem = tma_smem_bytes<RING, D, G>();
-        decode_tma_kernel<D, G, RING, ROPE><<<grid, kNW * 32, smem, st>>>(map, a);
-        return cudaGetLastError();
+        return launch_pdl(decode_tma_kernel<D, G, RING, ROPE>, grid, tma_smem_bytes<RING, D, G>(), st, map, a);
     }
 };
 
