@@ -86,6 +86,7 @@ def lib() -> C.CDLL:
         ("cottus_version", C.c_int, []),
         ("cottus_paged_decode_workspace_size", _sz, [P(PagedDecodeParams)]),
         ("cottus_paged_decode", C.c_int, [P(PagedDecodeParams), _vp]),
+        ("cottus_paged_decode_static_scratch", C.c_int, [P(PagedDecodeParams), _vp]),
         ("cottus_lse_combine", C.c_int, [P(LseCombineParams), _vp]),
         ("cottus_rope_cos_sin_fill", C.c_int, [_vp, _i32, _i32, _f32]),
         ("cottus_rope", C.c_int, [_vp, _vp, _vp, _i32, _i32, _i32, _vp, _i32, _vp]),

@@ -58,6 +58,11 @@ cudaError_t launch_decode_mma_d128(const DecodeDesc& d, cudaStream_t st);
 size_t mma_workers_d64(const DecodeDesc& d);
 size_t mma_workers_d128(const DecodeDesc& d);
 
+// Bytes at the start of a decode workspace that hold the pair arrival
+// counters (they must be zero before a launch that has never used the
+// workspace).  Used by the static-scratch entry point.
+size_t workspace_zero_prefix_bytes(int32_t batch, int32_t num_kv_heads);
+
 // Generic path: any head_dim <= 512, any block size; one CTA per (seq, head).
 cudaError_t launch_decode_generic(const DecodeDesc& d, cudaStream_t st);
 

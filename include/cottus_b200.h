@@ -103,6 +103,21 @@ typedef struct {
 size_t cottus_paged_decode_workspace_size(const cottus_paged_decode_params *p);
 int cottus_paged_decode(const cottus_paged_decode_params *p, cottus_stream_t stream);
 
+/* Allocation-free variant of cottus_paged_decode.  No counterpart in the
+ * reference.  For callers that cannot allocate device memory when attention
+ * runs (code inside an allocator or memory-pool callback, engines that
+ * reserve all device memory up front, plugin hosts that pass only a stream
+ * and the call's tensors): instead of a caller workspace it uses a 32 MiB
+ * scratch array compiled into the library, which every GPU that loads the
+ * library keeps until the process exits.  p->workspace and
+ * p->workspace_bytes are ignored.  Calls needing more scratch than 32 MiB
+ * (see cottus_paged_decode_workspace_size) fail with COTTUS_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address; make that
+ * first call before any stream capture.  All calls on a device share the
+ * array: calls whose executions overlap on the GPU race and must be ordered
+ * by the caller.  Nothing is allocated or freed. */
+int cottus_paged_decode_static_scratch(const cottus_paged_decode_params *p, cottus_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Split-KV merge of partial (normalised output, log-sum-exp) pairs produced
  * over disjoint context shards (e.g. one per GPU):
