@@ -99,35 +99,8 @@ __global__ void __launch_bounds__(kNW * 32)
     const long long W = (long long)gridDim.x * kNW;
     const long long w = (long long)blockIdx.x * kNW + warp;
     const WorkerPlan pl = plan_worker<D, ROPE>(a, w, W, lane);
-    const long long chunk = pl.chunk, u0 = pl.u0, u1 = pl.u1;
-    if (u0 >= u1) return;
-    const int nu = (int)(u1 - u0);
-    Cursor cur = pl.cur;
-
-    // ---- TMA issue (lane 0), block id prefetched one page ahead ----------
-    Cursor ic = cur;
-    int blk_next = lane == 0 ? a.bt[(long long)ic.b * a.maxb + ic.p] : 0;
-    auto issue = [&](int k) {
-        if (lane == 0) {
-            const int slot = k % RING;
-            const int blk = blk_next;
-            slot_blk[slot] = blk;
-            if (blk < 0 || (long long)blk >= a.num_blocks) {
-                mbar_arrive(&bars[slot]);
-            } else {
-                mbar_arrive_expect_tx(&bars[slot], C::SLOT_BYTES);
-                const int row0 = (blk * a.L + a.layer) * (2 * kBS);
-#pragma unroll
-                for (int r = 0; r < REG; ++r)
-                    tma_load_3d(slots + (size_t)slot * C::SLOT_BYTES + r * (32 * 128), &kv_map, &bars[slot], 64 * r,
-                                ic.h, row0);
-            }
-            cursor_next<ROPE>(ic, a);
-            if (k + 1 < nu) blk_next = a.bt[(long long)ic.b * a.maxb + ic.p];
-        }
-    };
-    const int prime = nu < RING ? nu : RING;
-    for (int k = 0; k < prime; ++k) issue(k);
+    const long long U = pl.U, chunk = pl.chunk;
+    const long long NC = (U + chunk - 1) / chunk;
 
     // fragment coordinates of this lane
     const int qc = lane & 3;   // column pair: heads 2qc, 2qc+1 of C fragments
@@ -140,8 +113,6 @@ __global__ void __launch_bounds__(kNW * 32)
     float o[KS][4];
     float qs[KS][4];  // raw query values of the next segment (loaded a page early)
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    bool seg_open = false, seg_first = true;
-    int seg_start_p = 0;
 
     // this lane's query elements of pair (b, h): head qr, dims kk*16 + 2qc + {0, 1, 8, 9}
     auto load_q = [&](int b, int h) {
@@ -163,237 +134,279 @@ __global__ void __launch_bounds__(kNW * 32)
             qs[kk][0] = u.x; qs[kk][1] = u.y; qs[kk][2] = v.x; qs[kk][3] = v.y;
         }
     };
-    load_q(cur.b, cur.h);
 
-    for (int k = 0; k < nu; ++k) {
-        const int slot = k % RING;
-        const int ctx_b = cur.n;
-        if (!seg_open) {
-            // ---- segment start: (rotate,) split and pack the staged query ----
-            seg_open = true;
-            seg_first = (k == 0);
-            seg_start_p = cur.p;
-            m0 = m1 = -INFINITY;
-            l0 = l1 = 0.f;
-            const bool live = qr < G;
-            const long long qrow = ((long long)cur.b * a.H + (long long)cur.h * G + (live ? qr : 0)) * D;
+    // ---- work: static chunk w, then chunks from the queue ------------------
+    long long cid = w < NC ? w : grab_chunk(a, W, NC, lane);
+    Cursor cur = pl.cur;
+    bool have_cur = w < NC;  // the plan located chunk w's first unit
+    int kg = 0;              // units consumed by this warp so far (ring slot / phase counter)
+
+    while (cid < NC) {
+        const long long u0 = cid * chunk, u1 = min(u0 + chunk, U);
+        const int nu = (int)(u1 - u0);
+        if (!have_cur) cur = locate_unit<ROPE>(a, u0, lane);
+        have_cur = false;
+
+        // ---- TMA issue (lane 0), block id prefetched one page ahead ----------
+        Cursor ic = cur;
+        int blk_next = lane == 0 ? a.bt[(long long)ic.b * a.maxb + ic.p] : 0;
+        auto issue = [&](int k) {
+            if (lane == 0) {
+                const int slot = (kg + k) % RING;
+                const int blk = blk_next;
+                slot_blk[slot] = blk;
+                if (blk < 0 || (long long)blk >= a.num_blocks) {
+                    mbar_arrive(&bars[slot]);
+                } else {
+                    mbar_arrive_expect_tx(&bars[slot], C::SLOT_BYTES);
+                    const int row0 = (blk * a.L + a.layer) * (2 * kBS);
 #pragma unroll
-            for (int kk = 0; kk < KS; ++kk) {
-                const int d0 = kk * 16 + 2 * qc, d1 = d0 + 8;
-                float x[4] = {qs[kk][0], qs[kk][1], qs[kk][2], qs[kk][3]};
-                if (ROPE && live) {
-                    const float* cs = a.cos_sin + (long long)(ctx_b - 1) * D;  // row of D/2 (cos, sin) pairs
-                    const float2 c0 = *reinterpret_cast<const float2*>(cs + d0);
-                    const float2 c1 = *reinterpret_cast<const float2*>(cs + d1);
-                    rope_pair(x[0], x[1], c0.x, c0.y, x[0], x[1]);
-                    rope_pair(x[2], x[3], c1.x, c1.y, x[2], x[3]);
-                    if (a.q_out && cur.p == 0) {
-                        if (a.q_f16) {
-                            *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d0) = pack_h2(x[0], x[1]);
-                            *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d1) = pack_h2(x[2], x[3]);
-                        } else {
-                            *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d0) = make_float2(x[0], x[1]);
-                            *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d1) = make_float2(x[2], x[3]);
+                    for (int r = 0; r < REG; ++r)
+                        tma_load_3d(slots + (size_t)slot * C::SLOT_BYTES + r * (32 * 128), &kv_map, &bars[slot], 64 * r,
+                                    ic.h, row0);
+                }
+                cursor_next<ROPE>(ic, a);
+                if (k + 1 < nu) blk_next = a.bt[(long long)ic.b * a.maxb + ic.p];
+            }
+        };
+        const int prime = nu < RING ? nu : RING;
+        for (int k = 0; k < prime; ++k) issue(k);
+        load_q(cur.b, cur.h);
+
+        bool seg_open = false, seg_first = true;
+        int seg_start_p = 0;
+        for (int k = 0; k < nu; ++k) {
+            const int slot = (kg + k) % RING;
+            const int ctx_b = cur.n;
+            if (!seg_open) {
+                // ---- segment start: (rotate,) split and pack the staged query ----
+                seg_open = true;
+                seg_first = (k == 0);
+                seg_start_p = cur.p;
+                m0 = m1 = -INFINITY;
+                l0 = l1 = 0.f;
+                const bool live = qr < G;
+                const long long qrow = ((long long)cur.b * a.H + (long long)cur.h * G + (live ? qr : 0)) * D;
+#pragma unroll
+                for (int kk = 0; kk < KS; ++kk) {
+                    const int d0 = kk * 16 + 2 * qc, d1 = d0 + 8;
+                    float x[4] = {qs[kk][0], qs[kk][1], qs[kk][2], qs[kk][3]};
+                    if (ROPE && live) {
+                        const float* cs = a.cos_sin + (long long)(ctx_b - 1) * D;  // row of D/2 (cos, sin) pairs
+                        const float2 c0 = *reinterpret_cast<const float2*>(cs + d0);
+                        const float2 c1 = *reinterpret_cast<const float2*>(cs + d1);
+                        rope_pair(x[0], x[1], c0.x, c0.y, x[0], x[1]);
+                        rope_pair(x[2], x[3], c1.x, c1.y, x[2], x[3]);
+                        if (a.q_out && cur.p == 0) {
+                            if (a.q_f16) {
+                                *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d0) = pack_h2(x[0], x[1]);
+                                *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d1) = pack_h2(x[2], x[3]);
+                            } else {
+                                *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d0) = make_float2(x[0], x[1]);
+                                *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d1) = make_float2(x[2], x[3]);
+                            }
                         }
                     }
+                    qb[kk][0] = pack_h2(x[0], x[1]);
+                    qb[kk][1] = pack_h2(x[2], x[3]);
+                    if constexpr (QSPLIT) {
+                        const float2 hA = unpack_h2(qb[kk][0]), hB = unpack_h2(qb[kk][1]);
+                        ql[kk][0] = pack_h2(x[0] - hA.x, x[1] - hA.y);
+                        ql[kk][1] = pack_h2(x[2] - hB.x, x[3] - hB.y);
+                    }
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) o[kk][i] = 0.f;
                 }
-                qb[kk][0] = pack_h2(x[0], x[1]);
-                qb[kk][1] = pack_h2(x[2], x[3]);
-                if constexpr (QSPLIT) {
-                    const float2 hA = unpack_h2(qb[kk][0]), hB = unpack_h2(qb[kk][1]);
-                    ql[kk][0] = pack_h2(x[0] - hA.x, x[1] - hA.y);
-                    ql[kk][1] = pack_h2(x[2] - hB.x, x[3] - hB.y);
+            }
+            if (cur.p == cur.np - 1 && k + 1 < nu) {
+                // this page ends the segment: stage the next pair's query now so
+                // the load latency hides behind this page's math
+                Cursor nx = cur;
+                cursor_next<ROPE>(nx, a);
+                load_q(nx.b, nx.h);
+            }
+
+            const bool landed = __all_sync(FULL, mbar_wait_bounded(&bars[slot], ((kg + k) / RING) & 1));
+            if (!landed) {
+                if (lane == 0) report(a.status, COTTUS_STATUS_TIMEOUT);
+                for (int kk = k + 1; kk < k + RING && kk < nu; ++kk)
+                    (void)__all_sync(FULL, mbar_wait_bounded(&bars[(kg + kk) % RING], ((kg + kk) / RING) & 1));
+                return;
+            }
+            const int blk = slot_blk[slot];
+            const bool blk_ok = blk >= 0 && (long long)blk < a.num_blocks;
+            if (!blk_ok && lane == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
+            int n_valid = blk_ok ? ctx_b - cur.p * kBS : 0;
+            n_valid = n_valid > kBS ? kBS : n_valid;
+            uint8_t* sl = slots + (size_t)slot * C::SLOT_BYTES;
+            const uint32_t sl_s = slots_s + (uint32_t)(slot * C::SLOT_BYTES);
+
+            if (ROPE && blk_ok && cur.p == cur.np - 1 && lane < LW) {
+                // the new token: rotate k, encode k and v (truncation), append
+                const int t_new = (ctx_b - 1) % kBS;
+                const long long src = ((long long)cur.b * a.Hkv + cur.h) * D + lane * 8;
+                float kx[8], vx[8];
+                if (a.q_f16) {
+                    load8(reinterpret_cast<const __half*>(a.k_new) + src, kx);
+                    load8(reinterpret_cast<const __half*>(a.v_new) + src, vx);
+                } else {
+                    load8(reinterpret_cast<const float*>(a.k_new) + src, kx);
+                    load8(reinterpret_cast<const float*>(a.v_new) + src, vx);
                 }
+                const float4* cs =
+                    reinterpret_cast<const float4*>(a.cos_sin + ((long long)(ctx_b - 1) * (D / 2) + lane * 4) * 2);
 #pragma unroll
-                for (int i = 0; i < 4; ++i) o[kk][i] = 0.f;
+                for (int pr = 0; pr < 2; ++pr) {
+                    const float4 c4 = __ldg(cs + pr);
+                    rope_pair(kx[4 * pr], kx[4 * pr + 1], c4.x, c4.y, kx[4 * pr], kx[4 * pr + 1]);
+                    rope_pair(kx[4 * pr + 2], kx[4 * pr + 3], c4.z, c4.w, kx[4 * pr + 2], kx[4 * pr + 3]);
+                }
+                uint32_t kw[4], vw[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    kw[j] = (uint32_t)f32_to_f16_trunc(kx[2 * j]) | ((uint32_t)f32_to_f16_trunc(kx[2 * j + 1]) << 16);
+                    vw[j] = (uint32_t)f32_to_f16_trunc(vx[2 * j]) | ((uint32_t)f32_to_f16_trunc(vx[2 * j + 1]) << 16);
+                }
+                const uint4 k4 = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+                const uint4 v4 = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+                *reinterpret_cast<uint4*>(sl + swz(lane / 8, t_new, lane % 8)) = k4;
+                *reinterpret_cast<uint4*>(sl + swz(lane / 8, kBS + t_new, lane % 8)) = v4;
+                const long long row0 = ((long long)blk * a.L + a.layer) * (2 * kBS);
+                *reinterpret_cast<uint4*>(a.kv + ((row0 + t_new) * a.Hkv + cur.h) * D + lane * 8) = k4;
+                *reinterpret_cast<uint4*>(a.kv + ((row0 + kBS + t_new) * a.Hkv + cur.h) * D + lane * 8) = v4;
             }
-        }
-        if (cur.p == cur.np - 1 && k + 1 < nu) {
-            // this page ends the segment: stage the next pair's query now so
-            // the load latency hides behind this page's math
-            Cursor nx = cur;
-            cursor_next<ROPE>(nx, a);
-            load_q(nx.b, nx.h);
-        }
+            if (n_valid < kBS) {
+                // V rows past the context may hold any bits (NaN, inf); zero them
+                // so that 0-probability tokens contribute exactly 0
+                const int nz = (kBS - n_valid) * REG * 8;  // 16-byte chunks
+                for (int i = lane; i < nz; i += 32) {
+                    const int row = n_valid + i / (REG * 8), rc = i % (REG * 8);
+                    *reinterpret_cast<uint4*>(sl + swz(rc / 8, kBS + row, rc % 8)) = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            if (ROPE || n_valid < kBS) __syncwarp();
 
-        const bool landed = __all_sync(FULL, mbar_wait_bounded(&bars[slot], (k / RING) & 1));
-        if (!landed) {
-            if (lane == 0) report(a.status, COTTUS_STATUS_TIMEOUT);
-            for (int kk = k + 1; kk < k + RING && kk < nu; ++kk)
-                (void)__all_sync(FULL, mbar_wait_bounded(&bars[kk % RING], (kk / RING) & 1));
-            return;
-        }
-        const int blk = slot_blk[slot];
-        const bool blk_ok = blk >= 0 && (long long)blk < a.num_blocks;
-        if (!blk_ok && lane == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
-        int n_valid = blk_ok ? ctx_b - cur.p * kBS : 0;
-        n_valid = n_valid > kBS ? kBS : n_valid;
-        uint8_t* sl = slots + (size_t)slot * C::SLOT_BYTES;
-        const uint32_t sl_s = slots_s + (uint32_t)(slot * C::SLOT_BYTES);
-
-        if (ROPE && blk_ok && cur.p == cur.np - 1 && lane < LW) {
-            // the new token: rotate k, encode k and v (truncation), append
-            const int t_new = (ctx_b - 1) % kBS;
-            const long long src = ((long long)cur.b * a.Hkv + cur.h) * D + lane * 8;
-            float kx[8], vx[8];
-            if (a.q_f16) {
-                load8(reinterpret_cast<const __half*>(a.k_new) + src, kx);
-                load8(reinterpret_cast<const __half*>(a.v_new) + src, vx);
-            } else {
-                load8(reinterpret_cast<const float*>(a.k_new) + src, kx);
-                load8(reinterpret_cast<const float*>(a.v_new) + src, vx);
-            }
-            const float4* cs =
-                reinterpret_cast<const float4*>(a.cos_sin + ((long long)(ctx_b - 1) * (D / 2) + lane * 4) * 2);
+            // ---- S^T = K . Q^T ----------------------------------------------------
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
+            {
+                const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+                const int csel = lane >> 4;
 #pragma unroll
-            for (int pr = 0; pr < 2; ++pr) {
-                const float4 c4 = __ldg(cs + pr);
-                rope_pair(kx[4 * pr], kx[4 * pr + 1], c4.x, c4.y, kx[4 * pr], kx[4 * pr + 1]);
-                rope_pair(kx[4 * pr + 2], kx[4 * pr + 3], c4.z, c4.w, kx[4 * pr + 2], kx[4 * pr + 3]);
+                for (int kk = 0; kk < KS; ++kk) {
+                    uint32_t af[4];
+                    ldsm_x4(sl_s + swz(kk / 4, row, (kk % 4) * 2 + csel), af);
+                    mma16816(s, af, qb[kk][0], qb[kk][1]);
+                    if constexpr (QSPLIT) mma16816(s, af, ql[kk][0], ql[kk][1]);
+                }
             }
-            uint32_t kw[4], vw[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                kw[j] = (uint32_t)f32_to_f16_trunc(kx[2 * j]) | ((uint32_t)f32_to_f16_trunc(kx[2 * j + 1]) << 16);
-                vw[j] = (uint32_t)f32_to_f16_trunc(vx[2 * j]) | ((uint32_t)f32_to_f16_trunc(vx[2 * j + 1]) << 16);
-            }
-            const uint4 k4 = make_uint4(kw[0], kw[1], kw[2], kw[3]);
-            const uint4 v4 = make_uint4(vw[0], vw[1], vw[2], vw[3]);
-            *reinterpret_cast<uint4*>(sl + swz(lane / 8, t_new, lane % 8)) = k4;
-            *reinterpret_cast<uint4*>(sl + swz(lane / 8, kBS + t_new, lane % 8)) = v4;
-            const long long row0 = ((long long)blk * a.L + a.layer) * (2 * kBS);
-            *reinterpret_cast<uint4*>(a.kv + ((row0 + t_new) * a.Hkv + cur.h) * D + lane * 8) = k4;
-            *reinterpret_cast<uint4*>(a.kv + ((row0 + kBS + t_new) * a.Hkv + cur.h) * D + lane * 8) = v4;
-        }
-        if (n_valid < kBS) {
-            // V rows past the context may hold any bits (NaN, inf); zero them
-            // so that 0-probability tokens contribute exactly 0
-            const int nz = (kBS - n_valid) * REG * 8;  // 16-byte chunks
-            for (int i = lane; i < nz; i += 32) {
-                const int row = n_valid + i / (REG * 8), rc = i % (REG * 8);
-                *reinterpret_cast<uint4*>(sl + swz(rc / 8, kBS + row, rc % 8)) = make_uint4(0u, 0u, 0u, 0u);
-            }
-        }
-        if (ROPE || n_valid < kBS) __syncwarp();
-
-        // ---- S^T = K . Q^T ----------------------------------------------------
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-        {
-            const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-            const int csel = lane >> 4;
-#pragma unroll
-            for (int kk = 0; kk < KS; ++kk) {
-                uint32_t af[4];
-                ldsm_x4(sl_s + swz(kk / 4, row, (kk % 4) * 2 + csel), af);
-                mma16816(s, af, qb[kk][0], qb[kk][1]);
-                if constexpr (QSPLIT) mma16816(s, af, ql[kk][0], ql[kk][1]);
-            }
-        }
-        // ---- online softmax on the fragment -----------------------------------
-        const bool ok0 = qr < n_valid, ok1 = qr + 8 < n_valid;
-        const float s00 = ok0 ? s[0] * a.qscale : -INFINITY, s01 = ok0 ? s[1] * a.qscale : -INFINITY;
-        const float s10 = ok1 ? s[2] * a.qscale : -INFINITY, s11 = ok1 ? s[3] * a.qscale : -INFINITY;
-        float c0 = fmaxf(s00, s10), c1 = fmaxf(s01, s11);
-#pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-            c0 = fmaxf(c0, __shfl_xor_sync(FULL, c0, off));
-            c1 = fmaxf(c1, __shfl_xor_sync(FULL, c1, off));
-        }
-        if (c0 > m0 + 8.0f) {
-            const float al = exp2f(m0 - c0);
-            m0 = c0;
-            l0 *= al;
-#pragma unroll
-            for (int j = 0; j < KS; ++j) {
-                o[j][0] *= al;
-                o[j][2] *= al;
-            }
-        }
-        if (c1 > m1 + 8.0f) {
-            const float al = exp2f(m1 - c1);
-            m1 = c1;
-            l1 *= al;
-#pragma unroll
-            for (int j = 0; j < KS; ++j) {
-                o[j][1] *= al;
-                o[j][3] *= al;
-            }
-        }
-        const float p00 = ok0 ? exp2f(s00 - m0) : 0.f, p01 = ok0 ? exp2f(s01 - m1) : 0.f;
-        const float p10 = ok1 ? exp2f(s10 - m0) : 0.f, p11 = ok1 ? exp2f(s11 - m1) : 0.f;
-        l0 += p00 + p10;
-        l1 += p01 + p11;
-        const uint32_t pb0 = movmatrix_trans(pack_h2(p00, p01));  // tokens 0-7
-        const uint32_t pb1 = movmatrix_trans(pack_h2(p10, p11));  // tokens 8-15
-
-        // ---- O^T += V^T . P^T --------------------------------------------------
-        {
-            const int tok = (lane & 7) + ((lane >> 4) & 1) * 8;
-            const int csel = (lane >> 3) & 1;
-#pragma unroll
-            for (int j = 0; j < KS; ++j) {
-                uint32_t af[4];
-                ldsm_x4_t(sl_s + swz(j / 4, kBS + tok, (j % 4) * 2 + csel), af);
-                mma16816(o[j], af, pb0, pb1);
-            }
-        }
-        __syncwarp();
-
-        if (k + RING < nu) {
-            fence_proxy_async_smem();
-            issue(k + RING);
-        }
-
-        const bool seg_end = (cur.p == cur.np - 1) || (k == nu - 1);
-        if (seg_end) {
-            float lt0 = l0, lt1 = l1;
+            // ---- online softmax on the fragment -----------------------------------
+            const bool ok0 = qr < n_valid, ok1 = qr + 8 < n_valid;
+            const float s00 = ok0 ? s[0] * a.qscale : -INFINITY, s01 = ok0 ? s[1] * a.qscale : -INFINITY;
+            const float s10 = ok1 ? s[2] * a.qscale : -INFINITY, s11 = ok1 ? s[3] * a.qscale : -INFINITY;
+            float c0 = fmaxf(s00, s10), c1 = fmaxf(s01, s11);
 #pragma unroll
             for (int off = 4; off < 32; off <<= 1) {
-                lt0 += __shfl_xor_sync(FULL, lt0, off);
-                lt1 += __shfl_xor_sync(FULL, lt1, off);
+                c0 = fmaxf(c0, __shfl_xor_sync(FULL, c0, off));
+                c1 = fmaxf(c1, __shfl_xor_sync(FULL, c1, off));
             }
-            const bool whole = seg_start_p == 0 && cur.p == cur.np - 1;
-            const long long slot_id = seg_first ? 2 * w : 2 * w + 1;
+            if (c0 > m0 + 8.0f) {
+                const float al = exp2f(m0 - c0);
+                m0 = c0;
+                l0 *= al;
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int g = hh ? h1 : h0;
-                if (g >= G) continue;
-                const float mg = hh ? m1 : m0, lg = hh ? lt1 : lt0;
-                const long long head = (long long)cur.b * a.H + (long long)cur.h * G + g;
-                if (whole) {
-                    const float inv = lg > 0.f ? 1.0f / lg : 0.f;
-#pragma unroll
-                    for (int j = 0; j < KS; ++j) {
-                        const float x0 = o[j][hh] * inv, x1 = o[j][2 + hh] * inv;
-                        const long long e0 = head * D + j * 16 + qr;
-                        if (a.out_f16) {
-                            reinterpret_cast<__half*>(a.out)[e0] = __float2half_rn(x0);
-                            reinterpret_cast<__half*>(a.out)[e0 + 8] = __float2half_rn(x1);
-                        } else {
-                            reinterpret_cast<float*>(a.out)[e0] = x0;
-                            reinterpret_cast<float*>(a.out)[e0 + 8] = x1;
-                        }
-                    }
-                    if (a.lse && qr == 0) a.lse[head] = lg > 0.f ? (mg + log2f(lg)) * kLn2 : -INFINITY;
-                } else {
-                    float* dst = a.ws_o + (slot_id * G + g) * D;
-#pragma unroll
-                    for (int j = 0; j < KS; ++j) {
-                        dst[j * 16 + qr] = o[j][hh];
-                        dst[j * 16 + qr + 8] = o[j][2 + hh];
-                    }
-                    if (qr == 0) {
-                        a.ws_ml[(slot_id * G + g) * 2] = mg;
-                        a.ws_ml[(slot_id * G + g) * 2 + 1] = lg;
-                    }
+                for (int j = 0; j < KS; ++j) {
+                    o[j][0] *= al;
+                    o[j][2] *= al;
                 }
             }
-            if (!whole)
-                merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, lane / LW, lane % LW);
+            if (c1 > m1 + 8.0f) {
+                const float al = exp2f(m1 - c1);
+                m1 = c1;
+                l1 *= al;
+#pragma unroll
+                for (int j = 0; j < KS; ++j) {
+                    o[j][1] *= al;
+                    o[j][3] *= al;
+                }
+            }
+            const float p00 = ok0 ? exp2f(s00 - m0) : 0.f, p01 = ok0 ? exp2f(s01 - m1) : 0.f;
+            const float p10 = ok1 ? exp2f(s10 - m0) : 0.f, p11 = ok1 ? exp2f(s11 - m1) : 0.f;
+            l0 += p00 + p10;
+            l1 += p01 + p11;
+            const uint32_t pb0 = movmatrix_trans(pack_h2(p00, p01));  // tokens 0-7
+            const uint32_t pb1 = movmatrix_trans(pack_h2(p10, p11));  // tokens 8-15
+
+            // ---- O^T += V^T . P^T --------------------------------------------------
+            {
+                const int tok = (lane & 7) + ((lane >> 4) & 1) * 8;
+                const int csel = (lane >> 3) & 1;
+#pragma unroll
+                for (int j = 0; j < KS; ++j) {
+                    uint32_t af[4];
+                    ldsm_x4_t(sl_s + swz(j / 4, kBS + tok, (j % 4) * 2 + csel), af);
+                    mma16816(o[j], af, pb0, pb1);
+                }
+            }
             __syncwarp();
-            seg_open = false;
+
+            if (k + RING < nu) {
+                fence_proxy_async_smem();
+                issue(k + RING);
+            }
+
+            const bool seg_end = (cur.p == cur.np - 1) || (k == nu - 1);
+            if (seg_end) {
+                float lt0 = l0, lt1 = l1;
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    lt0 += __shfl_xor_sync(FULL, lt0, off);
+                    lt1 += __shfl_xor_sync(FULL, lt1, off);
+                }
+                const bool whole = seg_start_p == 0 && cur.p == cur.np - 1;
+                const long long slot_id = seg_first ? 2 * cid : 2 * cid + 1;
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const int g = hh ? h1 : h0;
+                    if (g >= G) continue;
+                    const float mg = hh ? m1 : m0, lg = hh ? lt1 : lt0;
+                    const long long head = (long long)cur.b * a.H + (long long)cur.h * G + g;
+                    if (whole) {
+                        const float inv = lg > 0.f ? 1.0f / lg : 0.f;
+#pragma unroll
+                        for (int j = 0; j < KS; ++j) {
+                            const float x0 = o[j][hh] * inv, x1 = o[j][2 + hh] * inv;
+                            const long long e0 = head * D + j * 16 + qr;
+                            if (a.out_f16) {
+                                reinterpret_cast<__half*>(a.out)[e0] = __float2half_rn(x0);
+                                reinterpret_cast<__half*>(a.out)[e0 + 8] = __float2half_rn(x1);
+                            } else {
+                                reinterpret_cast<float*>(a.out)[e0] = x0;
+                                reinterpret_cast<float*>(a.out)[e0 + 8] = x1;
+                            }
+                        }
+                        if (a.lse && qr == 0) a.lse[head] = lg > 0.f ? (mg + log2f(lg)) * kLn2 : -INFINITY;
+                    } else {
+                        float* dst = a.ws_o + (slot_id * G + g) * D;
+#pragma unroll
+                        for (int j = 0; j < KS; ++j) {
+                            dst[j * 16 + qr] = o[j][hh];
+                            dst[j * 16 + qr + 8] = o[j][2 + hh];
+                        }
+                        if (qr == 0) {
+                            a.ws_ml[(slot_id * G + g) * 2] = mg;
+                            a.ws_ml[(slot_id * G + g) * 2 + 1] = lg;
+                        }
+                    }
+                }
+                if (!whole)
+                    merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, lane / LW, lane % LW);
+                __syncwarp();
+                seg_open = false;
+            }
+            if (k + 1 < nu) cursor_next<ROPE>(cur, a);
         }
-        if (k + 1 < nu) cursor_next<ROPE>(cur, a);
+        kg += nu;
+        cid = grab_chunk(a, W, NC, lane);
     }
 }
 

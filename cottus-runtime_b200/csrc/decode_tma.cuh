@@ -41,7 +41,16 @@ namespace cb200 {
 
 constexpr int kBS = 16;   // tokens per page on the fast path
 constexpr int kNW = 4;    // worker warps per CTA
-constexpr int kMinChunk = 8;  // fewest pages a worker takes (limits partials on tiny batches)
+constexpr int kMinChunk = 8;  // fewest pages in a chunk (limits partials on tiny batches)
+#ifndef CB200_CHUNKS_PER_WORKER
+#define CB200_CHUNKS_PER_WORKER 1
+#endif
+// Chunks per worker on average: each worker takes one static chunk, then
+// grabs more from a queue, so warps that stream slower take less work.
+// Measured on B200 (Llama-3-8B and 131k-context shapes): 1 is fastest;
+// 2, 3, 4 lose 10-45% because every chunk restarts the page ring from empty
+// and cuts its pairs into extra partials.
+constexpr int kChunksPerWorker = CB200_CHUNKS_PER_WORKER;
 
 struct TmaArgs {
     void* out;
@@ -212,8 +221,8 @@ __device__ __forceinline__ Cursor locate_unit(const TmaArgs& a, long long u, int
     return c;
 }
 
-// This worker's share of the launch: total units U, chunk size, its unit
-// range [u0, u1) and the cursor at u0.  For batches up to kPlanRegs*32
+// This worker's static share of the launch: total units U, chunk size, the
+// unit range [u0, u1) of chunk w and the cursor at u0.  For batches up to kPlanRegs*32
 // sequences the page counts are loaded once into registers and both the
 // total and the start position come from them; larger batches fall back to
 // repeated scans.  Also zero-fills the outputs of sequences without pages.
@@ -233,7 +242,7 @@ __device__ __forceinline__ WorkerPlan plan_worker(const TmaArgs& a, long long w,
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) total_pages += __shfl_xor_sync(FULL, total_pages, o);
         pl.U = total_pages * a.Hkv;
-        pl.chunk = max((pl.U + W - 1) / W, (long long)kMinChunk);
+        pl.chunk = max((pl.U + W * kChunksPerWorker - 1) / (W * kChunksPerWorker), (long long)kMinChunk);
         pl.u0 = min(w * pl.chunk, pl.U);
         pl.u1 = min(pl.u0 + pl.chunk, pl.U);
         zero_empty_sequences<D, ROPE>(a, w, W, lane);
@@ -252,7 +261,7 @@ __device__ __forceinline__ WorkerPlan plan_worker(const TmaArgs& a, long long w,
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(FULL, total, o);
     pl.U = total * a.Hkv;
-    pl.chunk = max((pl.U + W - 1) / W, (long long)kMinChunk);
+    pl.chunk = max((pl.U + W * kChunksPerWorker - 1) / (W * kChunksPerWorker), (long long)kMinChunk);
     pl.u0 = min(w * pl.chunk, pl.U);
     pl.u1 = min(pl.u0 + pl.chunk, pl.U);
     // worker i < kPlanRegs zero-fills the empty sequences among 32i .. 32i+31
@@ -313,6 +322,24 @@ __device__ __forceinline__ WorkerPlan plan_worker(const TmaArgs& a, long long w,
     return pl;
 }
 
+// Next chunk id for this warp: chunks 0..W-1 are taken statically by
+// workers 0..W-1, chunks W.. are handed out by a ticket counter (one word
+// at the start of the workspace, zero at launch start).  Every warp stops
+// at its first ticket past the last chunk, so exactly W such tickets are
+// drawn; the warp that draws the last of them resets the counter to zero
+// for the next launch on this workspace.  A plain atomicAdd per grab keeps
+// the queue contention-free even when every warp grabs at once.
+__device__ __forceinline__ long long grab_chunk(const TmaArgs& a, long long W, long long NC, int lane) {
+    long long id = 0;
+    if (lane == 0) {
+        const long long ticket = (long long)atomicAdd(a.counters, 1ull);
+        const long long ndyn = NC > W ? NC - W : 0;
+        id = W + ticket;
+        if (ticket == ndyn + W - 1) atomicExch(a.counters, 0ull);
+    }
+    return __shfl_sync(0xffffffffu, id, 0);
+}
+
 // Called by a worker after it stored its partial of a cut (sequence, kv
 // head) pair whose units are [ps, ps + np).  Worker wk owns units
 // [wk*chunk, (wk+1)*chunk), so the pair's partials belong to workers
@@ -330,7 +357,7 @@ __device__ __forceinline__ void merge_if_last(const TmaArgs& a, int b, int h, lo
     const long long w0 = ps / chunk, w1 = (ps + np - 1) / chunk;
     const int nparts = (int)(w1 - w0 + 1);
     const long long slot0 = w0 * chunk >= ps ? 2 * w0 : 2 * w0 + 1;  // later parts start inside the pair
-    unsigned long long* ctr = a.counters + (long long)b * a.Hkv + h;
+    unsigned long long* ctr = a.counters + 1 + (long long)b * a.Hkv + h;
     int last = 0;
     __syncwarp();
     if (lane == 0) {
@@ -445,295 +472,307 @@ __global__ void __launch_bounds__(kNW * 32)
     grid_dependency_wait();
     grid_dependents_launch();
 
-    // ---- this worker's unit range --------------------------------------
+    // ---- work: static chunk w, then chunks from the queue ----------------
     const long long W = (long long)gridDim.x * kNW;
     const long long w = (long long)blockIdx.x * kNW + warp;
     const WorkerPlan pl = plan_worker<D, ROPE>(a, w, W, lane);
-    const long long chunk = pl.chunk, u0 = pl.u0, u1 = pl.u1;
-    if (u0 >= u1) return;
-    const int nu = (int)(u1 - u0);
-    Cursor cur = pl.cur;
-
-    // ---- TMA issue: lane 0 owns the issue cursor; the block id of the next
-    // unit to issue is loaded one page ahead so its latency hides behind math.
-    Cursor ic = cur;
-    int blk_next = lane == 0 ? a.bt[(long long)ic.b * a.maxb + ic.p] : 0;
-    auto issue = [&](int k) {
-        if (lane == 0) {
-            const int slot = k % RING;
-            const int blk = blk_next;
-            slot_blk[slot] = blk;
-            if (blk < 0 || (long long)blk >= a.num_blocks) {
-                mbar_arrive(&bars[slot]);  // nothing to load; the consumer masks the page
-            } else {
-                mbar_arrive_expect_tx(&bars[slot], C::SLOT_BYTES);
-                tma_load_3d(slots + (size_t)slot * C::SLOT_BYTES, &kv_map, &bars[slot], 0, ic.h,
-                            (blk * a.L + a.layer) * (2 * kBS));
-            }
-            cursor_next<ROPE>(ic, a);
-            if (k + 1 < nu) blk_next = a.bt[(long long)ic.b * a.maxb + ic.p];
-        }
-    };
-    const int prime = nu < RING ? nu : RING;
-    for (int k = 0; k < prime; ++k) issue(k);
+    const long long U = pl.U, chunk = pl.chunk;
+    const long long NC = (U + chunk - 1) / chunk;
 
     float2 q2[G][4];
     float2 o2[G][4];
     float m_run = -INFINITY, l_own = 0.f;
-    bool seg_open = false;
-    int seg_start_p = 0;
-    bool seg_first = true;
     const int i0 = (lq * N) / LW;   // first partial index this lane holds after the reduction
     const int gl = i0 / STEPS;      // the head this lane scores
 
-    for (int k = 0; k < nu; ++k) {
-        const int slot = k % RING;
-        const int ctx_b = cur.n;
-        if (!seg_open) {
-            // ---- segment start: load (and rotate) the group's query rows ----
-            seg_open = true;
-            seg_first = (k == 0);
-            seg_start_p = cur.p;
-            m_run = -INFINITY;
-            l_own = 0.f;
+    long long cid = w < NC ? w : grab_chunk(a, W, NC, lane);
+    Cursor cur = pl.cur;
+    bool have_cur = w < NC;
+    int kg = 0;  // units consumed by this warp so far (ring slot / phase counter)
+
+    while (cid < NC) {
+        const long long u0 = cid * chunk, u1 = min(u0 + chunk, U);
+        const int nu = (int)(u1 - u0);
+        if (!have_cur) cur = locate_unit<ROPE>(a, u0, lane);
+        have_cur = false;
+
+        // ---- TMA issue: lane 0 owns the issue cursor; the block id of the next
+        // unit to issue is loaded one page ahead so its latency hides behind math.
+        Cursor ic = cur;
+        int blk_next = lane == 0 ? a.bt[(long long)ic.b * a.maxb + ic.p] : 0;
+        auto issue = [&](int k) {
+            if (lane == 0) {
+                const int slot = (kg + k) % RING;
+                const int blk = blk_next;
+                slot_blk[slot] = blk;
+                if (blk < 0 || (long long)blk >= a.num_blocks) {
+                    mbar_arrive(&bars[slot]);  // nothing to load; the consumer masks the page
+                } else {
+                    mbar_arrive_expect_tx(&bars[slot], C::SLOT_BYTES);
+                    tma_load_3d(slots + (size_t)slot * C::SLOT_BYTES, &kv_map, &bars[slot], 0, ic.h,
+                                (blk * a.L + a.layer) * (2 * kBS));
+                }
+                cursor_next<ROPE>(ic, a);
+                if (k + 1 < nu) blk_next = a.bt[(long long)ic.b * a.maxb + ic.p];
+            }
+        };
+        const int prime = nu < RING ? nu : RING;
+        for (int k = 0; k < prime; ++k) issue(k);
+
+        bool seg_open = false;
+        int seg_start_p = 0;
+        bool seg_first = true;
+        for (int k = 0; k < nu; ++k) {
+            const int slot = (kg + k) % RING;
+            const int ctx_b = cur.n;
+            if (!seg_open) {
+                // ---- segment start: load (and rotate) the group's query rows ----
+                seg_open = true;
+                seg_first = (k == 0);
+                seg_start_p = cur.p;
+                m_run = -INFINITY;
+                l_own = 0.f;
 #pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const long long row = ((long long)cur.b * a.H + (long long)cur.h * G + g) * D + lq * 8;
-                float x[8];
-                if (a.q_f16) load8(reinterpret_cast<const __half*>(a.q) + row, x);
-                else load8(reinterpret_cast<const float*>(a.q) + row, x);
-                if (ROPE) {
-                    const float4* cs = reinterpret_cast<const float4*>(
-                        a.cos_sin + ((long long)(ctx_b - 1) * (D / 2) + lq * 4) * 2);
+                for (int g = 0; g < G; ++g) {
+                    const long long row = ((long long)cur.b * a.H + (long long)cur.h * G + g) * D + lq * 8;
+                    float x[8];
+                    if (a.q_f16) load8(reinterpret_cast<const __half*>(a.q) + row, x);
+                    else load8(reinterpret_cast<const float*>(a.q) + row, x);
+                    if (ROPE) {
+                        const float4* cs = reinterpret_cast<const float4*>(
+                            a.cos_sin + ((long long)(ctx_b - 1) * (D / 2) + lq * 4) * 2);
 #pragma unroll
-                    for (int pr = 0; pr < 2; ++pr) {
-                        const float4 c4 = __ldg(cs + pr);
-                        rope_pair(x[4 * pr], x[4 * pr + 1], c4.x, c4.y, x[4 * pr], x[4 * pr + 1]);
-                        rope_pair(x[4 * pr + 2], x[4 * pr + 3], c4.z, c4.w, x[4 * pr + 2], x[4 * pr + 3]);
+                        for (int pr = 0; pr < 2; ++pr) {
+                            const float4 c4 = __ldg(cs + pr);
+                            rope_pair(x[4 * pr], x[4 * pr + 1], c4.x, c4.y, x[4 * pr], x[4 * pr + 1]);
+                            rope_pair(x[4 * pr + 2], x[4 * pr + 3], c4.z, c4.w, x[4 * pr + 2], x[4 * pr + 3]);
+                        }
+                        if (a.q_out && cur.p == 0 && grp == 0) {
+                            if (a.q_f16) store8(reinterpret_cast<__half*>(a.q_out) + row, x);
+                            else store8(reinterpret_cast<float*>(a.q_out) + row, x);
+                        }
                     }
-                    if (a.q_out && cur.p == 0 && grp == 0) {
-                        if (a.q_f16) store8(reinterpret_cast<__half*>(a.q_out) + row, x);
-                        else store8(reinterpret_cast<float*>(a.q_out) + row, x);
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    q2[g][j] = make_float2(x[2 * j] * a.qscale, x[2 * j + 1] * a.qscale);
-                    o2[g][j] = make_float2(0.f, 0.f);
-                }
-            }
-        }
-
-        const bool landed = __all_sync(FULL, mbar_wait_bounded(&bars[slot], (k / RING) & 1));
-        if (!landed) {
-            if (lane == 0) report(a.status, COTTUS_STATUS_TIMEOUT);
-            // let the loads still in flight land (bounded) before the warp leaves
-            for (int kk = k + 1; kk < k + RING && kk < nu; ++kk)
-                (void)__all_sync(FULL, mbar_wait_bounded(&bars[kk % RING], (kk / RING) & 1));
-            return;
-        }
-        const int blk = slot_blk[slot];
-        const bool blk_ok = blk >= 0 && (long long)blk < a.num_blocks;
-        if (!blk_ok && lane == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
-        int n_valid = blk_ok ? ctx_b - cur.p * kBS : 0;
-        n_valid = n_valid > kBS ? kBS : n_valid;
-        const uint16_t* kt = reinterpret_cast<const uint16_t*>(slots + (size_t)slot * C::SLOT_BYTES);
-        const uint16_t* vt = kt + kBS * D;
-
-        if (ROPE && blk_ok && cur.p == cur.np - 1 && grp == 0) {
-            // ---- the new token: rotate k, encode k and v, append -------------
-            const int t_new = (ctx_b - 1) % kBS;
-            const long long src = ((long long)cur.b * a.Hkv + cur.h) * D + lq * 8;
-            float kx[8], vx[8];
-            if (a.q_f16) {
-                load8(reinterpret_cast<const __half*>(a.k_new) + src, kx);
-                load8(reinterpret_cast<const __half*>(a.v_new) + src, vx);
-            } else {
-                load8(reinterpret_cast<const float*>(a.k_new) + src, kx);
-                load8(reinterpret_cast<const float*>(a.v_new) + src, vx);
-            }
-            const float4* cs =
-                reinterpret_cast<const float4*>(a.cos_sin + ((long long)(ctx_b - 1) * (D / 2) + lq * 4) * 2);
-#pragma unroll
-            for (int pr = 0; pr < 2; ++pr) {
-                const float4 c4 = __ldg(cs + pr);
-                rope_pair(kx[4 * pr], kx[4 * pr + 1], c4.x, c4.y, kx[4 * pr], kx[4 * pr + 1]);
-                rope_pair(kx[4 * pr + 2], kx[4 * pr + 3], c4.z, c4.w, kx[4 * pr + 2], kx[4 * pr + 3]);
-            }
-            uint32_t kw[4], vw[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                kw[j] = (uint32_t)f32_to_f16_trunc(kx[2 * j]) | ((uint32_t)f32_to_f16_trunc(kx[2 * j + 1]) << 16);
-                vw[j] = (uint32_t)f32_to_f16_trunc(vx[2 * j]) | ((uint32_t)f32_to_f16_trunc(vx[2 * j + 1]) << 16);
-            }
-            const uint4 k4 = make_uint4(kw[0], kw[1], kw[2], kw[3]);
-            const uint4 v4 = make_uint4(vw[0], vw[1], vw[2], vw[3]);
-            *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kt) + t_new * D + lq * 8) = k4;
-            *reinterpret_cast<uint4*>(const_cast<uint16_t*>(vt) + t_new * D + lq * 8) = v4;
-            const long long row0 = ((long long)blk * a.L + a.layer) * (2 * kBS);
-            const long long koff = ((row0 + t_new) * a.Hkv + cur.h) * D + lq * 8;
-            const long long voff = ((row0 + kBS + t_new) * a.Hkv + cur.h) * D + lq * 8;
-            *reinterpret_cast<uint4*>(a.kv + koff) = k4;
-            *reinterpret_cast<uint4*>(a.kv + voff) = v4;
-        }
-        if (ROPE) __syncwarp();
-
-        // ---- the page, CH tokens at a time ------------------------------------
-#pragma unroll
-        for (int c = 0; c < C::NCH; ++c) {
-            const int tb = c * CH;
-            float part[N];
-#pragma unroll
-            for (int s = 0; s < STEPS; ++s) {
-                const int row = tb + s * RPS + grp;
-                const uint4 raw = *reinterpret_cast<const uint4*>(kt + row * D + lq * 8);
-                const float2 k0 = h2_to_f2(raw.x), k1 = h2_to_f2(raw.y), k2 = h2_to_f2(raw.z),
-                             k3 = h2_to_f2(raw.w);
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    float2 acc = fmul2(q2[g][0], k0);
-                    acc = ffma2(q2[g][1], k1, acc);
-                    acc = ffma2(q2[g][2], k2, acc);
-                    acc = ffma2(q2[g][3], k3, acc);
-                    part[g * STEPS + s] = acc.x + acc.y;
-                }
-            }
-            TransposeReduce<N, LW / 2>::run(part, lq);
-
-            // scores of this lane (head gl), masked past the context
-            float sc[NV];
-            bool ok[NV];
-            float cmax = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < NV; ++j) {
-                const int s = (i0 + j) % STEPS;
-                const int t = tb + s * RPS + grp;
-                ok[j] = t < n_valid;
-                sc[j] = ok[j] ? part[j] : -INFINITY;
-                cmax = fmaxf(cmax, sc[j]);
-            }
-#pragma unroll
-            for (int o = 1; o < CL; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(FULL, cmax, o));
-#pragma unroll
-            for (int o = LW; o < 32; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(FULL, cmax, o));
-
-            const bool upd = cmax > m_run + 8.0f;
-            if (__any_sync(FULL, upd)) {
-                const float m_new = upd ? cmax : m_run;
-                const float alpha = upd ? exp2f(m_run - m_new) : 1.0f;
-                l_own *= alpha;
-                m_run = m_new;
-                if (grp == 0 && (lq % CL) == 0) hs[gl] = alpha;
-                __syncwarp();
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float al = hs[g];
-                    const float2 al2 = make_float2(al, al);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) o2[g][j] = fmul2(o2[g][j], al2);
-                }
-                __syncwarp();
-            }
-            float psum = 0.f;
-#pragma unroll
-            for (int j = 0; j < NV; ++j) {
-                const float pj = ok[j] ? exp2f(sc[j] - m_run) : 0.f;
-                psum += pj;
-                const int s = (i0 + j) % STEPS;
-                p_s[(grp * STEPS + s) * G + gl] = pj;
-            }
-            if (DUP == 1 || (lq % DUP) == 0) l_own += psum;
-            __syncwarp();
-
-#pragma unroll
-            for (int s = 0; s < STEPS; ++s) {
-                const int row = tb + s * RPS + grp;
-                uint4 raw = *reinterpret_cast<const uint4*>(vt + row * D + lq * 8);
-                if (row >= n_valid) raw = make_uint4(0u, 0u, 0u, 0u);
-                const float2 v0 = h2_to_f2(raw.x), v1 = h2_to_f2(raw.y), v2 = h2_to_f2(raw.z),
-                             v3 = h2_to_f2(raw.w);
-                float pv[G];
-#pragma unroll
-                for (int g = 0; g < G; ++g) pv[g] = p_s[(grp * STEPS + s) * G + g];
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float2 p2 = make_float2(pv[g], pv[g]);
-                    o2[g][0] = ffma2(p2, v0, o2[g][0]);
-                    o2[g][1] = ffma2(p2, v1, o2[g][1]);
-                    o2[g][2] = ffma2(p2, v2, o2[g][2]);
-                    o2[g][3] = ffma2(p2, v3, o2[g][3]);
-                }
-            }
-            __syncwarp();
-        }
-
-        // ---- refill this slot --------------------------------------------
-        if (k + RING < nu) {
-            fence_proxy_async_smem();
-            issue(k + RING);
-        }
-
-        // ---- segment end -------------------------------------------------
-        const bool seg_end = (cur.p == cur.np - 1) || (k == nu - 1);
-        if (seg_end) {
-#pragma unroll
-            for (int o = LW; o < 32; o <<= 1) {
-#pragma unroll
-                for (int g = 0; g < G; ++g) {
 #pragma unroll
                     for (int j = 0; j < 4; ++j) {
-                        o2[g][j].x += __shfl_xor_sync(FULL, o2[g][j].x, o);
-                        o2[g][j].y += __shfl_xor_sync(FULL, o2[g][j].y, o);
+                        q2[g][j] = make_float2(x[2 * j] * a.qscale, x[2 * j + 1] * a.qscale);
+                        o2[g][j] = make_float2(0.f, 0.f);
                     }
                 }
             }
-            float lt = l_own;
-#pragma unroll
-            for (int o = 1; o < CL; o <<= 1) lt += __shfl_xor_sync(FULL, lt, o);
-#pragma unroll
-            for (int o = LW; o < 32; o <<= 1) lt += __shfl_xor_sync(FULL, lt, o);
-            if (grp == 0 && (lq % CL) == 0) {
-                hs[2 * gl] = m_run;
-                hs[2 * gl + 1] = lt;
+
+            const bool landed = __all_sync(FULL, mbar_wait_bounded(&bars[slot], ((kg + k) / RING) & 1));
+            if (!landed) {
+                if (lane == 0) report(a.status, COTTUS_STATUS_TIMEOUT);
+                // let the loads still in flight land (bounded) before the warp leaves
+                for (int kk = k + 1; kk < k + RING && kk < nu; ++kk)
+                    (void)__all_sync(FULL, mbar_wait_bounded(&bars[(kg + kk) % RING], ((kg + kk) / RING) & 1));
+                return;
             }
-            __syncwarp();
-            const bool whole = seg_start_p == 0 && cur.p == cur.np - 1;
-            if (grp == 0) {
-                const long long slot_id = seg_first ? 2 * w : 2 * w + 1;
+            const int blk = slot_blk[slot];
+            const bool blk_ok = blk >= 0 && (long long)blk < a.num_blocks;
+            if (!blk_ok && lane == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
+            int n_valid = blk_ok ? ctx_b - cur.p * kBS : 0;
+            n_valid = n_valid > kBS ? kBS : n_valid;
+            const uint16_t* kt = reinterpret_cast<const uint16_t*>(slots + (size_t)slot * C::SLOT_BYTES);
+            const uint16_t* vt = kt + kBS * D;
+
+            if (ROPE && blk_ok && cur.p == cur.np - 1 && grp == 0) {
+                // ---- the new token: rotate k, encode k and v, append -------------
+                const int t_new = (ctx_b - 1) % kBS;
+                const long long src = ((long long)cur.b * a.Hkv + cur.h) * D + lq * 8;
+                float kx[8], vx[8];
+                if (a.q_f16) {
+                    load8(reinterpret_cast<const __half*>(a.k_new) + src, kx);
+                    load8(reinterpret_cast<const __half*>(a.v_new) + src, vx);
+                } else {
+                    load8(reinterpret_cast<const float*>(a.k_new) + src, kx);
+                    load8(reinterpret_cast<const float*>(a.v_new) + src, vx);
+                }
+                const float4* cs =
+                    reinterpret_cast<const float4*>(a.cos_sin + ((long long)(ctx_b - 1) * (D / 2) + lq * 4) * 2);
 #pragma unroll
-                for (int g = 0; g < G; ++g) {
-                    const float mg = hs[2 * g], lg = hs[2 * g + 1];
-                    const long long head = (long long)cur.b * a.H + (long long)cur.h * G + g;
-                    float x[8];
-                    if (whole) {
-                        const float inv = lg > 0.f ? 1.0f / lg : 0.f;
+                for (int pr = 0; pr < 2; ++pr) {
+                    const float4 c4 = __ldg(cs + pr);
+                    rope_pair(kx[4 * pr], kx[4 * pr + 1], c4.x, c4.y, kx[4 * pr], kx[4 * pr + 1]);
+                    rope_pair(kx[4 * pr + 2], kx[4 * pr + 3], c4.z, c4.w, kx[4 * pr + 2], kx[4 * pr + 3]);
+                }
+                uint32_t kw[4], vw[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    kw[j] = (uint32_t)f32_to_f16_trunc(kx[2 * j]) | ((uint32_t)f32_to_f16_trunc(kx[2 * j + 1]) << 16);
+                    vw[j] = (uint32_t)f32_to_f16_trunc(vx[2 * j]) | ((uint32_t)f32_to_f16_trunc(vx[2 * j + 1]) << 16);
+                }
+                const uint4 k4 = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+                const uint4 v4 = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+                *reinterpret_cast<uint4*>(const_cast<uint16_t*>(kt) + t_new * D + lq * 8) = k4;
+                *reinterpret_cast<uint4*>(const_cast<uint16_t*>(vt) + t_new * D + lq * 8) = v4;
+                const long long row0 = ((long long)blk * a.L + a.layer) * (2 * kBS);
+                const long long koff = ((row0 + t_new) * a.Hkv + cur.h) * D + lq * 8;
+                const long long voff = ((row0 + kBS + t_new) * a.Hkv + cur.h) * D + lq * 8;
+                *reinterpret_cast<uint4*>(a.kv + koff) = k4;
+                *reinterpret_cast<uint4*>(a.kv + voff) = v4;
+            }
+            if (ROPE) __syncwarp();
+
+            // ---- the page, CH tokens at a time ------------------------------------
+#pragma unroll
+            for (int c = 0; c < C::NCH; ++c) {
+                const int tb = c * CH;
+                float part[N];
+#pragma unroll
+                for (int s = 0; s < STEPS; ++s) {
+                    const int row = tb + s * RPS + grp;
+                    const uint4 raw = *reinterpret_cast<const uint4*>(kt + row * D + lq * 8);
+                    const float2 k0 = h2_to_f2(raw.x), k1 = h2_to_f2(raw.y), k2 = h2_to_f2(raw.z),
+                                 k3 = h2_to_f2(raw.w);
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        float2 acc = fmul2(q2[g][0], k0);
+                        acc = ffma2(q2[g][1], k1, acc);
+                        acc = ffma2(q2[g][2], k2, acc);
+                        acc = ffma2(q2[g][3], k3, acc);
+                        part[g * STEPS + s] = acc.x + acc.y;
+                    }
+                }
+                TransposeReduce<N, LW / 2>::run(part, lq);
+
+                // scores of this lane (head gl), masked past the context
+                float sc[NV];
+                bool ok[NV];
+                float cmax = -INFINITY;
+#pragma unroll
+                for (int j = 0; j < NV; ++j) {
+                    const int s = (i0 + j) % STEPS;
+                    const int t = tb + s * RPS + grp;
+                    ok[j] = t < n_valid;
+                    sc[j] = ok[j] ? part[j] : -INFINITY;
+                    cmax = fmaxf(cmax, sc[j]);
+                }
+#pragma unroll
+                for (int o = 1; o < CL; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(FULL, cmax, o));
+#pragma unroll
+                for (int o = LW; o < 32; o <<= 1) cmax = fmaxf(cmax, __shfl_xor_sync(FULL, cmax, o));
+
+                const bool upd = cmax > m_run + 8.0f;
+                if (__any_sync(FULL, upd)) {
+                    const float m_new = upd ? cmax : m_run;
+                    const float alpha = upd ? exp2f(m_run - m_new) : 1.0f;
+                    l_own *= alpha;
+                    m_run = m_new;
+                    if (grp == 0 && (lq % CL) == 0) hs[gl] = alpha;
+                    __syncwarp();
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const float al = hs[g];
+                        const float2 al2 = make_float2(al, al);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) o2[g][j] = fmul2(o2[g][j], al2);
+                    }
+                    __syncwarp();
+                }
+                float psum = 0.f;
+#pragma unroll
+                for (int j = 0; j < NV; ++j) {
+                    const float pj = ok[j] ? exp2f(sc[j] - m_run) : 0.f;
+                    psum += pj;
+                    const int s = (i0 + j) % STEPS;
+                    p_s[(grp * STEPS + s) * G + gl] = pj;
+                }
+                if (DUP == 1 || (lq % DUP) == 0) l_own += psum;
+                __syncwarp();
+
+#pragma unroll
+                for (int s = 0; s < STEPS; ++s) {
+                    const int row = tb + s * RPS + grp;
+                    uint4 raw = *reinterpret_cast<const uint4*>(vt + row * D + lq * 8);
+                    if (row >= n_valid) raw = make_uint4(0u, 0u, 0u, 0u);
+                    const float2 v0 = h2_to_f2(raw.x), v1 = h2_to_f2(raw.y), v2 = h2_to_f2(raw.z),
+                                 v3 = h2_to_f2(raw.w);
+                    float pv[G];
+#pragma unroll
+                    for (int g = 0; g < G; ++g) pv[g] = p_s[(grp * STEPS + s) * G + g];
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const float2 p2 = make_float2(pv[g], pv[g]);
+                        o2[g][0] = ffma2(p2, v0, o2[g][0]);
+                        o2[g][1] = ffma2(p2, v1, o2[g][1]);
+                        o2[g][2] = ffma2(p2, v2, o2[g][2]);
+                        o2[g][3] = ffma2(p2, v3, o2[g][3]);
+                    }
+                }
+                __syncwarp();
+            }
+
+            // ---- refill this slot --------------------------------------------
+            if (k + RING < nu) {
+                fence_proxy_async_smem();
+                issue(k + RING);
+            }
+
+            // ---- segment end -------------------------------------------------
+            const bool seg_end = (cur.p == cur.np - 1) || (k == nu - 1);
+            if (seg_end) {
+#pragma unroll
+                for (int o = LW; o < 32; o <<= 1) {
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            x[2 * j] = o2[g][j].x * inv;
-                            x[2 * j + 1] = o2[g][j].y * inv;
-                        }
-                        if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + head * D + lq * 8, x);
-                        else store8(reinterpret_cast<float*>(a.out) + head * D + lq * 8, x);
-                        if (a.lse && lq == 0) a.lse[head] = lg > 0.f ? (mg + log2f(lg)) * kLn2 : -INFINITY;
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 4; ++j) {
-                            x[2 * j] = o2[g][j].x;
-                            x[2 * j + 1] = o2[g][j].y;
-                        }
-                        store8(a.ws_o + (slot_id * G + g) * D + lq * 8, x);
-                        if (lq == 0) {
-                            a.ws_ml[(slot_id * G + g) * 2] = mg;
-                            a.ws_ml[(slot_id * G + g) * 2 + 1] = lg;
+                            o2[g][j].x += __shfl_xor_sync(FULL, o2[g][j].x, o);
+                            o2[g][j].y += __shfl_xor_sync(FULL, o2[g][j].y, o);
                         }
                     }
                 }
+                float lt = l_own;
+#pragma unroll
+                for (int o = 1; o < CL; o <<= 1) lt += __shfl_xor_sync(FULL, lt, o);
+#pragma unroll
+                for (int o = LW; o < 32; o <<= 1) lt += __shfl_xor_sync(FULL, lt, o);
+                if (grp == 0 && (lq % CL) == 0) {
+                    hs[2 * gl] = m_run;
+                    hs[2 * gl + 1] = lt;
+                }
+                __syncwarp();
+                const bool whole = seg_start_p == 0 && cur.p == cur.np - 1;
+                if (grp == 0) {
+                    const long long slot_id = seg_first ? 2 * cid : 2 * cid + 1;
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const float mg = hs[2 * g], lg = hs[2 * g + 1];
+                        const long long head = (long long)cur.b * a.H + (long long)cur.h * G + g;
+                        float x[8];
+                        if (whole) {
+                            const float inv = lg > 0.f ? 1.0f / lg : 0.f;
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                x[2 * j] = o2[g][j].x * inv;
+                                x[2 * j + 1] = o2[g][j].y * inv;
+                            }
+                            if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + head * D + lq * 8, x);
+                            else store8(reinterpret_cast<float*>(a.out) + head * D + lq * 8, x);
+                            if (a.lse && lq == 0) a.lse[head] = lg > 0.f ? (mg + log2f(lg)) * kLn2 : -INFINITY;
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 4; ++j) {
+                                x[2 * j] = o2[g][j].x;
+                                x[2 * j + 1] = o2[g][j].y;
+                            }
+                            store8(a.ws_o + (slot_id * G + g) * D + lq * 8, x);
+                            if (lq == 0) {
+                                a.ws_ml[(slot_id * G + g) * 2] = mg;
+                                a.ws_ml[(slot_id * G + g) * 2 + 1] = lg;
+                            }
+                        }
+                    }
+                }
+                if (!whole) merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, grp, lq);
+                __syncwarp();
+                seg_open = false;
             }
-            if (!whole) merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, grp, lq);
-            __syncwarp();
-            seg_open = false;
+            if (k + 1 < nu) cursor_next<ROPE>(cur, a);
         }
-        if (k + 1 < nu) cursor_next<ROPE>(cur, a);
+        kg += nu;
+        cid = grab_chunk(a, W, NC, lane);
     }
 }
 
@@ -743,6 +782,9 @@ __global__ void __launch_bounds__(kNW * 32)
 CUtensorMap make_kv_tensor_map(const DecodeDesc& d, bool swizzle128, cudaError_t* err);
 int device_sm_count(int device);
 unsigned next_epoch();
+
+// Upper bound on the number of chunks of a launch with W workers.
+inline long long max_chunks(long long W) { return W * kChunksPerWorker + 1; }
 
 // Launch with programmatic stream serialization: the kernel may begin its
 // prologue while the previous kernel of the stream drains; it waits
@@ -763,8 +805,9 @@ inline cudaError_t launch_pdl(Kern kern, int grid, size_t smem, cudaStream_t st,
     return cudaLaunchKernelEx(&cfg, kern, map, a);
 }
 
-// Kernel arguments of one launch; the workspace holds the pair counters,
-// then 2*W partial slots of G x D outputs and G x (m, l).
+// Kernel arguments of one launch; the workspace holds the chunk queue word
+// and the pair counters, then 2 partial slots per chunk of G x D outputs
+// and G x (m, l).
 inline TmaArgs make_tma_args(const DecodeDesc& d, long long W, int G, int D) {
     TmaArgs a;
     a.out = d.out;
@@ -773,10 +816,10 @@ inline TmaArgs make_tma_args(const DecodeDesc& d, long long W, int G, int D) {
     a.ctx = d.context_lens;
     a.positions = d.positions;
     a.lse = d.lse;
-    const size_t ctr_bytes = ((size_t)d.batch * d.num_kv_heads * 8 + 255) & ~size_t(255);
+    const size_t ctr_bytes = workspace_zero_prefix_bytes(d.batch, d.num_kv_heads);
     a.counters = reinterpret_cast<unsigned long long*>(d.workspace);
     a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(d.workspace) + ctr_bytes);
-    a.ws_ml = a.ws_o + (size_t)2 * W * G * D;
+    a.ws_ml = a.ws_o + (size_t)2 * max_chunks(W) * G * D;
     a.status = d.status;
     a.k_new = d.k_new;
     a.v_new = d.v_new;

@@ -82,6 +82,12 @@ CUtensorMap make_kv_tensor_map(const DecodeDesc& d, bool swizzle128, cudaError_t
     return map;
 }
 
+// Leading bytes of a decode workspace: the chunk queue word and one arrival
+// counter per (sequence, kv head) pair, rounded to 256 bytes.
+size_t workspace_zero_prefix_bytes(int32_t batch, int32_t num_kv_heads) {
+    return ((1 + (size_t)batch * (size_t)num_kv_heads) * 8 + 255) & ~size_t(255);
+}
+
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 bool tma_supported(const DecodeDesc& d) {
@@ -124,8 +130,8 @@ static size_t workers(const DecodeDesc& d) {
 size_t tma_workspace_bytes(const DecodeDesc& d) {
     const size_t W = workers(d);
     const size_t G = (size_t)(d.num_heads / d.num_kv_heads);
-    const size_t ctr_bytes = ((size_t)d.batch * d.num_kv_heads * 8 + 255) & ~size_t(255);
-    return ctr_bytes + 2 * W * G * ((size_t)d.head_dim + 2) * sizeof(float) + 256;
+    const size_t ctr_bytes = workspace_zero_prefix_bytes(d.batch, d.num_kv_heads);
+    return ctr_bytes + 2 * (size_t)max_chunks((long long)W) * G * ((size_t)d.head_dim + 2) * sizeof(float) + 256;
 }
 
 cudaError_t launch_decode_tma(const DecodeDesc& d, cudaStream_t st) {

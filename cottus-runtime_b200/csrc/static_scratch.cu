@@ -63,14 +63,6 @@ int scratch_address(void** out) {
 
 }  // namespace
 
-namespace cb200 {
-// Same layout as the workspace of the fast path (make_tma_args): the
-// counters of the batch's (sequence, kv head) pairs, rounded to 256 bytes.
-size_t workspace_zero_prefix_bytes(int32_t batch, int32_t num_kv_heads) {
-    return ((size_t)batch * (size_t)num_kv_heads * 8 + 255) & ~size_t(255);
-}
-}  // namespace cb200
-
 extern "C" int cottus_paged_decode_static_scratch(const cottus_paged_decode_params* p, cottus_stream_t stream) {
     if (!p) return cb200::set_error(COTTUS_ERR_INVALID_ARGUMENT, "params must not be NULL");
     const size_t need = cottus_paged_decode_workspace_size(p);

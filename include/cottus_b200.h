@@ -93,7 +93,9 @@ typedef struct {
      * normalised partial output and lse_out[b][h] its natural-log
      * log-sum-exp, for cottus_lse_combine across context shards. */
     float *lse_out;
-    void *workspace;            /* >= cottus_paged_decode_workspace_size() bytes, 256-B aligned */
+    void *workspace;            /* >= cottus_paged_decode_workspace_size() bytes, 16-B aligned, zero-filled
+                                   once after allocation (the kernels leave it zeroed; after a call that
+                                   reported COTTUS_STATUS_TIMEOUT, zero it again) */
     size_t workspace_bytes;
     uint32_t *status;           /* optional device word, COTTUS_STATUS_* bits */
 } cottus_paged_decode_params;
@@ -190,7 +192,7 @@ typedef struct {
     void *out;                  /* [batch][num_heads][head_dim], out_dtype */
     int32_t out_dtype;
     float scale;                /* <= 0: 1/sqrt(head_dim) */
-    void *workspace;
+    void *workspace;            /* as cottus_paged_decode_params.workspace */
     size_t workspace_bytes;
     uint32_t *status;           /* optional device word */
 } cottus_decode_step_params;
