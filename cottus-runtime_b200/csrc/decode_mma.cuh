@@ -69,8 +69,16 @@ constexpr size_t mma_smem_bytes() {
     return (size_t)kNW * RING * MmaCfg<D>::SLOT_BYTES + (size_t)kNW * RING * 8 + (size_t)kNW * RING * 4 + 1024;
 }
 
+// CTAs per SM the register budget is fitted to: three rings of pages per SM
+// keep more bytes in flight than two; the split-query and group-8 variants
+// need more registers and settle for two.
+template <int D, int G, bool QSPLIT>
+constexpr int mma_min_ctas() {
+    return (QSPLIT || G >= 8) ? 2 : 3;
+}
+
 template <int D, int G, int RING, bool ROPE, bool QSPLIT>
-__global__ void __launch_bounds__(kNW * 32)
+__global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D, G, QSPLIT>())
     decode_mma_kernel(const __grid_constant__ CUtensorMap kv_map, const TmaArgs a) {
     using C = MmaCfg<D>;
     constexpr int KS = C::KSTEPS, REG = C::REGIONS, LW = D / 8;
@@ -111,7 +119,10 @@ __global__ void __launch_bounds__(kNW * 32)
     uint32_t qb[KS][2];
     uint32_t ql[QSPLIT ? KS : 1][2];
     float o[KS][4];
-    float qs[KS][4];  // raw query values of the next segment (loaded a page early)
+    // query of the next segment, loaded a page early: raw fp32 values where
+    // they get split (fp32 or rotated queries), else the fp16 pairs as stored
+    float qs[QSPLIT ? KS : 1][4];
+    uint32_t qn[QSPLIT ? 1 : KS][2];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
     // this lane's query elements of pair (b, h): head qr, dims kk*16 + 2qc + {0, 1, 8, 9}
@@ -121,22 +132,28 @@ __global__ void __launch_bounds__(kNW * 32)
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
             const int d0 = kk * 16 + 2 * qc, d1 = d0 + 8;
-            float2 u = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
-            if (live) {
-                if (a.q_f16) {
-                    u = unpack_h2(__ldg(reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow + d0)));
-                    v = unpack_h2(__ldg(reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow + d1)));
-                } else {
-                    u = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d0));
-                    v = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d1));
+            if constexpr (!QSPLIT) {  // fp16 queries, kept packed
+                const unsigned* qh = reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow);
+                qn[kk][0] = live ? __ldg(qh + d0 / 2) : 0u;
+                qn[kk][1] = live ? __ldg(qh + d1 / 2) : 0u;
+            } else {
+                float2 u = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
+                if (live) {
+                    if (a.q_f16) {
+                        u = unpack_h2(__ldg(reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow + d0)));
+                        v = unpack_h2(__ldg(reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow + d1)));
+                    } else {
+                        u = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d0));
+                        v = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d1));
+                    }
                 }
+                qs[kk][0] = u.x; qs[kk][1] = u.y; qs[kk][2] = v.x; qs[kk][3] = v.y;
             }
-            qs[kk][0] = u.x; qs[kk][1] = u.y; qs[kk][2] = v.x; qs[kk][3] = v.y;
         }
     };
 
     // ---- work: static chunk w, then chunks from the queue ------------------
-    long long cid = w < NC ? w : grab_chunk(a, W, NC, lane);
+    long long cid = w < NC ? w : (NC > W ? grab_chunk(a, W, NC, lane) : NC);
     Cursor cur = pl.cur;
     bool have_cur = w < NC;  // the plan located chunk w's first unit
     int kg = 0;              // units consumed by this warp so far (ring slot / phase counter)
@@ -175,6 +192,7 @@ __global__ void __launch_bounds__(kNW * 32)
 
         bool seg_open = false, seg_first = true;
         int seg_start_p = 0;
+        unsigned long long ctr_hint = 0;  // arrival counter of the open segment's pair, read a page early
         for (int k = 0; k < nu; ++k) {
             const int slot = (kg + k) % RING;
             const int ctx_b = cur.n;
@@ -183,36 +201,42 @@ __global__ void __launch_bounds__(kNW * 32)
                 seg_open = true;
                 seg_first = (k == 0);
                 seg_start_p = cur.p;
+                ctr_hint = 0;
                 m0 = m1 = -INFINITY;
                 l0 = l1 = 0.f;
                 const bool live = qr < G;
                 const long long qrow = ((long long)cur.b * a.H + (long long)cur.h * G + (live ? qr : 0)) * D;
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
-                    const int d0 = kk * 16 + 2 * qc, d1 = d0 + 8;
-                    float x[4] = {qs[kk][0], qs[kk][1], qs[kk][2], qs[kk][3]};
-                    if (ROPE && live) {
-                        const float* cs = a.cos_sin + (long long)(ctx_b - 1) * D;  // row of D/2 (cos, sin) pairs
-                        const float2 c0 = *reinterpret_cast<const float2*>(cs + d0);
-                        const float2 c1 = *reinterpret_cast<const float2*>(cs + d1);
-                        rope_pair(x[0], x[1], c0.x, c0.y, x[0], x[1]);
-                        rope_pair(x[2], x[3], c1.x, c1.y, x[2], x[3]);
-                        if (a.q_out && cur.p == 0) {
-                            if (a.q_f16) {
-                                *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d0) = pack_h2(x[0], x[1]);
-                                *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d1) = pack_h2(x[2], x[3]);
-                            } else {
-                                *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d0) = make_float2(x[0], x[1]);
-                                *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d1) = make_float2(x[2], x[3]);
+                    if constexpr (!QSPLIT) {
+                        qb[kk][0] = qn[kk][0];
+                        qb[kk][1] = qn[kk][1];
+                    } else {
+                        const int d0 = kk * 16 + 2 * qc, d1 = d0 + 8;
+                        float x[4] = {qs[kk][0], qs[kk][1], qs[kk][2], qs[kk][3]};
+                        if (ROPE && live) {
+                            const float* cs = a.cos_sin + (long long)(ctx_b - 1) * D;  // row of D/2 (cos, sin) pairs
+                            const float2 c0 = *reinterpret_cast<const float2*>(cs + d0);
+                            const float2 c1 = *reinterpret_cast<const float2*>(cs + d1);
+                            rope_pair(x[0], x[1], c0.x, c0.y, x[0], x[1]);
+                            rope_pair(x[2], x[3], c1.x, c1.y, x[2], x[3]);
+                            if (a.q_out && cur.p == 0) {
+                                if (a.q_f16) {
+                                    *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d0) = pack_h2(x[0], x[1]);
+                                    *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d1) = pack_h2(x[2], x[3]);
+                                } else {
+                                    *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d0) = make_float2(x[0], x[1]);
+                                    *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d1) = make_float2(x[2], x[3]);
+                                }
                             }
                         }
-                    }
-                    qb[kk][0] = pack_h2(x[0], x[1]);
-                    qb[kk][1] = pack_h2(x[2], x[3]);
-                    if constexpr (QSPLIT) {
-                        const float2 hA = unpack_h2(qb[kk][0]), hB = unpack_h2(qb[kk][1]);
-                        ql[kk][0] = pack_h2(x[0] - hA.x, x[1] - hA.y);
-                        ql[kk][1] = pack_h2(x[2] - hB.x, x[3] - hB.y);
+                        qb[kk][0] = pack_h2(x[0], x[1]);
+                        qb[kk][1] = pack_h2(x[2], x[3]);
+                        if constexpr (QSPLIT) {
+                            const float2 hA = unpack_h2(qb[kk][0]), hB = unpack_h2(qb[kk][1]);
+                            ql[kk][0] = pack_h2(x[0] - hA.x, x[1] - hA.y);
+                            ql[kk][1] = pack_h2(x[2] - hB.x, x[3] - hB.y);
+                        }
                     }
 #pragma unroll
                     for (int i = 0; i < 4; ++i) o[kk][i] = 0.f;
@@ -354,6 +378,12 @@ __global__ void __launch_bounds__(kNW * 32)
                 issue(k + RING);
             }
 
+            // the next page ends a cut segment of this pair: read the pair's
+            // arrival counter now, so the arrival's compare-and-swap finds it
+            if (lane == 0 && k + 1 < nu && cur.p + 1 < cur.np && (cur.p + 2 == cur.np || k + 2 == nu) &&
+                !(seg_start_p == 0 && cur.p + 2 == cur.np))
+                ctr_hint = ld_relaxed_u64(a.counters + 1 + (long long)cur.b * a.Hkv + cur.h);
+
             const bool seg_end = (cur.p == cur.np - 1) || (k == nu - 1);
             if (seg_end) {
                 float lt0 = l0, lt1 = l1;
@@ -399,14 +429,14 @@ __global__ void __launch_bounds__(kNW * 32)
                     }
                 }
                 if (!whole)
-                    merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, lane / LW, lane % LW);
+                    merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, ctr_hint);
                 __syncwarp();
                 seg_open = false;
             }
             if (k + 1 < nu) cursor_next<ROPE>(cur, a);
         }
         kg += nu;
-        cid = grab_chunk(a, W, NC, lane);
+        cid = NC > W ? grab_chunk(a, W, NC, lane) : NC;
     }
 }
 

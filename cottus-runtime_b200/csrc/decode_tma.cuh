@@ -61,7 +61,7 @@ struct TmaArgs {
     float* lse;
     float* ws_o;
     float* ws_ml;
-    unsigned long long* counters;  // [B * Hkv] arrival counters of cut pairs, tagged with `epoch`
+    unsigned long long* counters;  // chunk queue word, then [B * Hkv] arrival counters tagged with `epoch`
     uint32_t* status;
     const void* k_new;
     const void* v_new;
@@ -344,26 +344,31 @@ __device__ __forceinline__ long long grab_chunk(const TmaArgs& a, long long W, l
 // head) pair whose units are [ps, ps + np).  Worker wk owns units
 // [wk*chunk, (wk+1)*chunk), so the pair's partials belong to workers
 // ps/chunk .. (ps+np-1)/chunk, every one of them non-empty.  Arrives on the
-// pair's counter (tagged with the launch epoch, so a count left by an
-// aborted launch reads as zero); the last arriving worker merges all
-// partials (loads spread over the lanes and issued independently) and
-// resets the counter to zero.
+// pair's counter, tagged with the launch epoch so that a count left by an
+// aborted launch, or bytes of another layout that used the same workspace,
+// read as zero: a compare-and-swap from `hint`, the counter value read a
+// page earlier, which is right on the first try unless another part arrived
+// in between.  The last arriving worker merges all partials.  Lane items
+// are (head, 8-dim chunk); each lane reads the parts PB at a time with all
+// their loads in flight together and folds them into a running (max, sum,
+// output), so PB parts cost one round trip to L2.
 template <int D, int G>
 __device__ __forceinline__ void merge_if_last(const TmaArgs& a, int b, int h, long long ps, int np, long long chunk,
-                                              int lane, int grp, int lq) {
+                                              int lane, unsigned long long hint) {
     constexpr unsigned FULL = 0xffffffffu;
-    (void)grp;
-    (void)lq;
+    constexpr int CPR = D / 8;     // 8-dim chunks per head row
+    constexpr int ITEMS = G * CPR;  // (head, chunk) items
+    constexpr int PB = 4;           // parts loaded together
     const long long w0 = ps / chunk, w1 = (ps + np - 1) / chunk;
     const int nparts = (int)(w1 - w0 + 1);
     const long long slot0 = w0 * chunk >= ps ? 2 * w0 : 2 * w0 + 1;  // later parts start inside the pair
     unsigned long long* ctr = a.counters + 1 + (long long)b * a.Hkv + h;
-    int last = 0;
+    fence_acq_rel_gpu();  // this lane's partial stores are visible device-wide before the arrival
     __syncwarp();
+    int last = 0;
     if (lane == 0) {
-        __threadfence();  // this worker's partial is visible before its arrival
-        unsigned long long old = atomicAdd(ctr, 0ull);
-        while (true) {
+        unsigned long long old = hint;
+        while (true) {  // every failed attempt means another part arrived: at most nparts rounds
             const unsigned long long nv =
                 (unsigned)(old >> 32) == a.epoch ? old + 1 : (((unsigned long long)a.epoch << 32) | 1ull);
             const unsigned long long prev = atomicCAS(ctr, old, nv);
@@ -373,69 +378,52 @@ __device__ __forceinline__ void merge_if_last(const TmaArgs& a, int b, int h, lo
             }
             old = prev;
         }
-        if (last) __threadfence();
+        if (last) fence_acq_rel_gpu();
     }
     last = __shfl_sync(FULL, last, 0);
-    __syncwarp();
     if (!last) return;
     auto slot_of = [&](int j) -> long long { return j == 0 ? slot0 : 2 * (w0 + j); };
-    // (1) per head: max and rescaled denominator over the parts.  Items
-    // (part j, head g) are spread over the lanes; lanes congruent mod G hold
-    // the same head, so a butterfly over the higher lane bits reduces them.
-    float M = -INFINITY, Ls = 0.f;
-    const int gi = lane % G;
-    for (int i = lane; i < nparts * G; i += 32)
-        M = fmaxf(M, __ldcg(a.ws_ml + (slot_of(i / G) * G + gi) * 2));
-#pragma unroll
-    for (int o = G; o < 32; o <<= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
-    for (int i = lane; i < nparts * G; i += 32) {
-        const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + (slot_of(i / G) * G + gi) * 2));
-        if (ml.x != -INFINITY) Ls += ml.y * exp2f(ml.x - M);
-    }
-#pragma unroll
-    for (int o = G; o < 32; o <<= 1) Ls += __shfl_xor_sync(FULL, Ls, o);
-    // every lane learns (M, Ls) of every head from lanes 0..G-1
-    float Mh[G], Lh[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-        Mh[g] = __shfl_sync(FULL, M, g);
-        Lh[g] = __shfl_sync(FULL, Ls, g);
-    }
-    // (2) outputs: items (head g, 8-dim chunk c) spread over the lanes; each
-    // lane sums its items over the parts with independent loads.
-    constexpr int CPR = D / 8;  // chunks per head row
 #pragma unroll 1
-    for (int it = lane; it < G * CPR; it += 32) {
+    for (int it = lane; it < ITEMS; it += 32) {
         const int g = it / CPR, c = it % CPR;
-        float Mg = Mh[0], Lg = Lh[0];
+        float M = -INFINITY, L = 0.f, acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+        for (int j0 = 0; j0 < nparts; j0 += PB) {
+            float2 ml[PB];
+            float4 x0[PB], x1[PB];
 #pragma unroll
-        for (int gg = 1; gg < G; ++gg)
-            if (g == gg) {
-                Mg = Mh[gg];
-                Lg = Lh[gg];
+            for (int q = 0; q < PB; ++q) {
+                ml[q] = make_float2(-INFINITY, 0.f);
+                x0[q] = x1[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (j0 + q < nparts) {
+                    const long long sl = slot_of(j0 + q);
+                    ml[q] = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + (sl * G + g) * 2));
+                    const float4* src = reinterpret_cast<const float4*>(a.ws_o + (sl * G + g) * D + c * 8);
+                    x0[q] = __ldcg(src);
+                    x1[q] = __ldcg(src + 1);
+                }
             }
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        if (Mg != -INFINITY) {
-#pragma unroll 4
-            for (int j = 0; j < nparts; ++j) {
-                const long long sl = slot_of(j);
-                const float m = __ldcg(a.ws_ml + (sl * G + g) * 2);
-                const float4* src = reinterpret_cast<const float4*>(a.ws_o + (sl * G + g) * D + c * 8);
-                const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
-                const float wgt = m == -INFINITY ? 0.f : exp2f(m - Mg);
-                acc[0] += wgt * x0.x; acc[1] += wgt * x0.y; acc[2] += wgt * x0.z; acc[3] += wgt * x0.w;
-                acc[4] += wgt * x1.x; acc[5] += wgt * x1.y; acc[6] += wgt * x1.z; acc[7] += wgt * x1.w;
+#pragma unroll
+            for (int q = 0; q < PB; ++q) {
+                const float m = ml[q].x;
+                if (m == -INFINITY) continue;  // a part without valid tokens (or past the last part)
+                const float Mn = fmaxf(M, m);
+                const float sa = exp2f(M - Mn), sb = exp2f(m - Mn);
+                M = Mn;
+                L = L * sa + ml[q].y * sb;
+                const float xv[8] = {x0[q].x, x0[q].y, x0[q].z, x0[q].w, x1[q].x, x1[q].y, x1[q].z, x1[q].w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] = acc[e] * sa + xv[e] * sb;
             }
         }
-        const float inv = Lg > 0.f ? 1.f / Lg : 0.f;
+        const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] *= inv;
+        for (int e = 0; e < 8; ++e) acc[e] *= inv;
         const long long head = (long long)b * a.H + (long long)h * G + g;
         if (a.out_f16) store8(reinterpret_cast<__half*>(a.out) + head * D + c * 8, acc);
         else store8(reinterpret_cast<float*>(a.out) + head * D + c * 8, acc);
-        if (a.lse && c == 0) a.lse[head] = Lg > 0.f ? (Mg + log2f(Lg)) * kLn2 : -INFINITY;
+        if (a.lse && c == 0) a.lse[head] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
     }
-    if (lane == 0) atomicExch(ctr, 0ull);
 }
 
 template <int D, int G, int RING, bool ROPE>
@@ -485,7 +473,7 @@ __global__ void __launch_bounds__(kNW * 32)
     const int i0 = (lq * N) / LW;   // first partial index this lane holds after the reduction
     const int gl = i0 / STEPS;      // the head this lane scores
 
-    long long cid = w < NC ? w : grab_chunk(a, W, NC, lane);
+    long long cid = w < NC ? w : (NC > W ? grab_chunk(a, W, NC, lane) : NC);
     Cursor cur = pl.cur;
     bool have_cur = w < NC;
     int kg = 0;  // units consumed by this warp so far (ring slot / phase counter)
@@ -522,6 +510,7 @@ __global__ void __launch_bounds__(kNW * 32)
         bool seg_open = false;
         int seg_start_p = 0;
         bool seg_first = true;
+        unsigned long long ctr_hint = 0;  // arrival counter of the open segment's pair, read a page early
         for (int k = 0; k < nu; ++k) {
             const int slot = (kg + k) % RING;
             const int ctx_b = cur.n;
@@ -530,6 +519,7 @@ __global__ void __launch_bounds__(kNW * 32)
                 seg_open = true;
                 seg_first = (k == 0);
                 seg_start_p = cur.p;
+                ctr_hint = 0;
                 m_run = -INFINITY;
                 l_own = 0.f;
 #pragma unroll
@@ -709,6 +699,12 @@ __global__ void __launch_bounds__(kNW * 32)
                 issue(k + RING);
             }
 
+            // the next page ends a cut segment of this pair: read the pair's
+            // arrival counter now, so the arrival's compare-and-swap finds it
+            if (lane == 0 && k + 1 < nu && cur.p + 1 < cur.np && (cur.p + 2 == cur.np || k + 2 == nu) &&
+                !(seg_start_p == 0 && cur.p + 2 == cur.np))
+                ctr_hint = ld_relaxed_u64(a.counters + 1 + (long long)cur.b * a.Hkv + cur.h);
+
             // ---- segment end -------------------------------------------------
             const bool seg_end = (cur.p == cur.np - 1) || (k == nu - 1);
             if (seg_end) {
@@ -765,14 +761,14 @@ __global__ void __launch_bounds__(kNW * 32)
                         }
                     }
                 }
-                if (!whole) merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, grp, lq);
+                if (!whole) merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, ctr_hint);
                 __syncwarp();
                 seg_open = false;
             }
             if (k + 1 < nu) cursor_next<ROPE>(cur, a);
         }
         kg += nu;
-        cid = grab_chunk(a, W, NC, lane);
+        cid = NC > W ? grab_chunk(a, W, NC, lane) : NC;
     }
 }
 
@@ -821,6 +817,7 @@ inline TmaArgs make_tma_args(const DecodeDesc& d, long long W, int G, int D) {
     a.ws_o = reinterpret_cast<float*>(static_cast<uint8_t*>(d.workspace) + ctr_bytes);
     a.ws_ml = a.ws_o + (size_t)2 * max_chunks(W) * G * D;
     a.status = d.status;
+    a.epoch = next_epoch();
     a.k_new = d.k_new;
     a.v_new = d.v_new;
     a.cos_sin = d.cos_sin;
@@ -836,7 +833,6 @@ inline TmaArgs make_tma_args(const DecodeDesc& d, long long W, int G, int D) {
     a.max_pos = d.max_position;
     a.q_f16 = d.q_f16;
     a.out_f16 = d.out_f16;
-    a.epoch = next_epoch();
     a.qscale = d.scale * kLog2e;
     return a;
 }

@@ -94,8 +94,8 @@ typedef struct {
      * log-sum-exp, for cottus_lse_combine across context shards. */
     float *lse_out;
     void *workspace;            /* >= cottus_paged_decode_workspace_size() bytes, 16-B aligned, zero-filled
-                                   once after allocation (the kernels leave it zeroed; after a call that
-                                   reported COTTUS_STATUS_TIMEOUT, zero it again) */
+                                   once after allocation (the kernels leave the words that must be zero at
+                                   zero; after a call that reported COTTUS_STATUS_TIMEOUT, zero it again) */
     size_t workspace_bytes;
     uint32_t *status;           /* optional device word, COTTUS_STATUS_* bits */
 } cottus_paged_decode_params;
