@@ -96,35 +96,67 @@ class ClockSampler:
 
 # -- CPU baseline (reference pagedAttentionCPU compiled from its sources) --------------------
 
+class ReferenceBatch:
+    """The reference's CPU path (oracle/_ref, pagedAttentionCPU) over sequences
+    of a workload, one call per sequence, spread over the host threads by the
+    library.  Host copies of the pages are made once, outside any timing."""
+
+    def __init__(self, w, t, max_seqs=None):
+        from oracle.oracle import Reference
+        from cottus_b200.workloads import host_subpool
+
+        self.ref, self.w = Reference(), w
+        self.threads = os.cpu_count() or 1
+        seqs = list(range(w.B if max_seqs is None else min(w.B, max_seqs)))
+        sub, bt, ctx = host_subpool(w, t["kv_pool"], seqs)
+        self.q = t["query"][seqs].float().cpu().numpy()
+        per = w.block_elems()
+        # the reference computes element offsets in int32 (paged_attention_cpu.cpp:63): rebase every
+        # sequence onto its own lowest block, or, where its blocks span too far for that, copy its
+        # pages into a buffer of their own in table order (identity table)
+        self.bases, self.bt, self.keep = [], bt.copy(), [sub]
+        for i in range(len(seqs)):
+            n = (int(ctx[i]) + w.bs - 1) // w.bs
+            lo = int(bt[i, :n].min()) if n else 0
+            hi = int(bt[i, :n].max()) if n else 0
+            if (hi - lo + 1) * per < 2 ** 31:
+                self.bases.append(sub.ctypes.data + 2 * lo * per)
+                self.bt[i, :n] -= lo
+            else:
+                own = np.ascontiguousarray(sub.reshape(-1, per)[bt[i, :n]])
+                self.keep.append(own)
+                self.bases.append(own.ctypes.data)
+                self.bt[i, :n] = np.arange(n, dtype=np.int32)
+        self.ctx = ctx
+        self.out = np.zeros((len(seqs), w.H * w.D), np.float32)
+
+    def lens(self, n, cap=None):
+        c = self.ctx[:n]
+        return c if cap is None else np.minimum(c, cap).astype(np.int32)
+
+    def kv_bytes(self, n, cap=None):
+        return int(np.sum(self.lens(n, cap).astype(np.int64))) * 2 * self.w.Hkv * self.w.D * 2
+
+    def run(self, n, cap=None):
+        """First n sequences; with `cap`, each over its first `cap` tokens only."""
+        w = self.w
+        self.ref.paged_attention_batch_rebased(self.out[:n], self.q[:n], self.bases[:n], self.bt[:n],
+                                               self.lens(n, cap), w.layer, w.H, w.Hkv, w.D, w.bs, w.L, self.threads)
+
+
 def cpu_reference_rate(w, t, target_s=8.0, max_seqs=None):
     """Times the reference's CPU path on the host cores over a sample of the
     workload's sequences; returns (GB/s, threads, sample description)."""
-    from oracle.oracle import Reference
-    from cottus_b200.workloads import host_subpool
-
-    ref = Reference()
-    threads = os.cpu_count() or 1
-    seqs = list(range(w.B if max_seqs is None else min(w.B, max_seqs)))
-    sub, bt, ctx = host_subpool(w, t["kv_pool"], seqs)
-    q = t["query"][seqs].float().cpu().numpy()
-    per = w.block_elems()
-    # rebase every sequence onto its own lowest block so int32 offsets stay in range
-    bases, bt2 = [], bt.copy()
-    for i in range(len(seqs)):
-        n = (int(ctx[i]) + w.bs - 1) // w.bs
-        lo = int(bt[i, :n].min()) if n else 0
-        bases.append(sub.ctypes.data + 2 * lo * per)
-        bt2[i, :n] -= lo
-    out = np.zeros((len(seqs), w.H * w.D), np.float32)
-    kvb = int(np.sum(ctx.astype(np.int64))) * 2 * w.Hkv * w.D * 2
+    rb = ReferenceBatch(w, t, max_seqs)
+    n = len(rb.ctx)
     reps, t0 = 0, time.perf_counter()
     while True:
-        ref.paged_attention_batch_rebased(out, q, bases, bt2, ctx, w.layer, w.H, w.Hkv, w.D, w.bs, w.L, threads)
+        rb.run(n)
         reps += 1
         el = time.perf_counter() - t0
         if el >= target_s or reps >= 1000:
             break
-    return kvb * reps / el / 1e9, threads, f"{len(seqs)} of {w.B} sequences x {reps} passes ({el:.1f} s wall)"
+    return rb.kv_bytes(n) * reps / el / 1e9, rb.threads, f"{n} of {w.B} sequences x {reps} passes ({el:.1f} s wall)"
 
 
 # -- main --------------------------------------------------------------------------------------
@@ -145,15 +177,31 @@ def run_reference(args, rank, world):
     from cottus_b200 import workloads as W
     w = build_workload(args.config, 0, args.batch)
     t = W.device_tensors(w, "cpu" if not torch.cuda.is_available() else "cuda")
-    # bounded per-step sample: whole batch when it is cheap, else a prefix of sequences
-    max_seqs = 64 if w.name != "long_ctx_70b" else 1
+    # each step is a bounded sample of the workload, sized from one timed sequence so that warm-up and
+    # timed steps together take about a minute (a few at most): the first n whole sequences, or, where one
+    # sequence alone takes longer than a step may, the first `cap` tokens of one sequence per thread
+    rb = ReferenceBatch(w, t, max_seqs=64)
+    c0 = int(min(int(rb.ctx[0]), 2048))
+    t1 = time.perf_counter()
+    rb.run(1, c0)
+    per_token = max(time.perf_counter() - t1, 1e-6) / c0
+    budget = min(2.0, 60.0 / max(args.steps + args.warmup, 1))  # per step; threads contend, so aim low
+    one = per_token * int(rb.ctx[0])
+    threads = rb.threads
+    if one <= budget:
+        n, cap = int(min(len(rb.ctx), (budget // one) * threads)), None
+        sample = f"first {n} of {w.B} sequences per step"
+    else:
+        n, cap = int(min(len(rb.ctx), threads)), int(max(w.bs, budget // per_token))
+        sample = f"first {cap} tokens of each of the first {n} of {w.B} sequences per step"
     rates = []
     for _ in range(args.warmup):
-        cpu_reference_rate(w, t, target_s=0.0, max_seqs=max_seqs)
+        rb.run(n, cap)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        r, threads, sample = cpu_reference_rate(w, t, target_s=0.0, max_seqs=max_seqs)
-        rates.append(r)
+        ts = time.perf_counter()
+        rb.run(n, cap)
+        rates.append(rb.kv_bytes(n, cap) / (time.perf_counter() - ts) / 1e9)
     el = time.perf_counter() - t0
     v = float(np.mean(rates))
     line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -354,7 +402,13 @@ def main():
     total_kv = (w.kv_bytes() if split else kv_bytes_rank * world)
     value = total_kv / (ms * 1e-3) / 1e9
     alg = kv_bytes_rank + wl.io_bytes()
-    achieved = alg / (k_ms * 1e-3) / 1e9
+    # launch duration for the roofline: where a step is one launch of the
+    # kernel, the timed region per launch (launches back to back, as a decode
+    # loop issues them); otherwise the kernel timed alone between events
+    kern_ms = ms if launches_per_step == 1 else k_ms
+    achieved = alg / (kern_ms * 1e-3) / 1e9
+    mma = (w.H // w.Hkv) > 1 and w.D in (64, 128) and (w.out_dtype == torch.float16 or split)
+    kname = ("decode_mma_kernel" if mma else "decode_tma_kernel") + (" (RoPE + append fused)" if w.fused else "")
     traffic = None
     prof = ROOT / "profiles" / "traffic.json"
     if prof.exists():
@@ -374,8 +428,8 @@ def main():
         "pct_hbm_peak": value / world / peak * 100 if not split else value / world / peak * 100,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": "decode_tma_kernel (one launch per cottus_paged_decode call)",
-                     "kernel_ms": k_ms, "algorithmic_bytes": alg},
+                     "kernel": kname + (" + lse_combine_kernel" if split else "") + ": one decode launch per step",
+                     "kernel_ms": kern_ms, "kernel_ms_alone": k_ms, "algorithmic_bytes": alg},
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
