@@ -61,6 +61,13 @@ class DecodeStepParams(C.Structure):
     ]
 
 
+class DecodeBatchDesc(C.Structure):
+    _fields_ = [
+        ("num_blocks", _i32), ("block_size", _i32), ("max_batch", _i32), ("max_blocks_per_seq", _i32),
+        ("device_block_table", _vp), ("device_positions", _vp),
+    ]
+
+
 class CottusError(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"{message} (code {code})")
@@ -101,6 +108,16 @@ def lib() -> C.CDLL:
         ("cottus_block_allocator_free", C.c_int, [_vp, _i32]),
         ("cottus_block_allocator_num_free", _i32, [_vp]),
         ("cottus_block_allocator_total_blocks", _i32, [_vp]),
+        ("cottus_decode_batch_create", C.c_int, [P(DecodeBatchDesc), P(_vp)]),
+        ("cottus_decode_batch_destroy", None, [_vp]),
+        ("cottus_decode_batch_add", C.c_int, [_vp, _i64, P(_i32)]),
+        ("cottus_decode_batch_release", C.c_int, [_vp, _i64]),
+        ("cottus_decode_batch_begin_step", C.c_int, [_vp, _vp]),
+        ("cottus_decode_batch_end_step", C.c_int, [_vp]),
+        ("cottus_decode_batch_size", _i32, [_vp]),
+        ("cottus_decode_batch_free_blocks", _i32, [_vp]),
+        ("cottus_decode_batch_rows", C.c_int, [_vp, P(_i64), _i32]),
+        ("cottus_decode_batch_sequence", C.c_int, [_vp, _i64, P(_i32), P(_i32), P(_i32), _i32, P(_i32)]),
     ]
     for name, res, args in sig:
         fn = getattr(L, name)

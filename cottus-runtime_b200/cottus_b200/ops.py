@@ -11,7 +11,8 @@ import ctypes as C
 import torch
 
 from . import _lib
-from ._lib import (F16, F32, CottusError, DecodeStepParams, LseCombineParams, PagedDecodeParams, check, lib)
+from ._lib import (F16, F32, CottusError, DecodeBatchDesc, DecodeStepParams, LseCombineParams, PagedDecodeParams, check,
+                   lib)
 
 _DT = {torch.float32: F32, torch.float16: F16}
 
@@ -242,4 +243,71 @@ class BlockAllocator:
         h = getattr(self, "_h", None)
         if h:
             lib().cottus_block_allocator_destroy(h)
+            self._h = None
+
+
+class DecodeBatch:
+    """Batched decode-step driver (cottus_decode_batch_*): the block
+    bookkeeping of Engine::generate (engine.cpp:52-95) for many sequences,
+    with the block table and positions resident on the device.
+
+    `device` None keeps the host bookkeeping only.  Per step:
+    ``begin_step()``, then per layer ``rope_append_decode(...)`` with
+    ``block_table=self.block_table[:n]``, ``positions=self.positions[:n]``
+    (n = len(self)), then ``end_step()``."""
+
+    def __init__(self, num_blocks: int, block_size: int, max_batch: int, max_blocks_per_seq: int, device=None):
+        self.block_table = self.positions = None
+        d = DecodeBatchDesc()
+        d.num_blocks, d.block_size, d.max_batch, d.max_blocks_per_seq = num_blocks, block_size, max_batch, \
+            max_blocks_per_seq
+        if device is not None:
+            self.block_table = torch.zeros((max_batch, max_blocks_per_seq), dtype=torch.int32, device=device)
+            self.positions = torch.zeros(max_batch, dtype=torch.int32, device=device)
+            d.device_block_table, d.device_positions = self.block_table.data_ptr(), self.positions.data_ptr()
+        h = C.c_void_p()
+        check(lib().cottus_decode_batch_create(C.byref(d), C.byref(h)))
+        self._h = h
+        self.max_batch, self.max_blocks_per_seq = max_batch, max_blocks_per_seq
+
+    def add(self, seq_id: int) -> int:
+        row = C.c_int32()
+        check(lib().cottus_decode_batch_add(self._h, int(seq_id), C.byref(row)))
+        return row.value
+
+    def release(self, seq_id: int) -> None:
+        check(lib().cottus_decode_batch_release(self._h, int(seq_id)))
+
+    def begin_step(self, stream=None) -> None:
+        check(lib().cottus_decode_batch_begin_step(self._h, _stream(stream) if self.block_table is not None
+                                                    else None))
+
+    def end_step(self) -> None:
+        check(lib().cottus_decode_batch_end_step(self._h))
+
+    def __len__(self) -> int:
+        return int(lib().cottus_decode_batch_size(self._h))
+
+    def free_blocks(self) -> int:
+        return int(lib().cottus_decode_batch_free_blocks(self._h))
+
+    def rows(self) -> list:
+        n = len(self)
+        ids = (C.c_int64 * max(n, 1))()
+        lib().cottus_decode_batch_rows(self._h, ids, n)
+        return [int(ids[i]) for i in range(n)]
+
+    def sequence(self, seq_id: int):
+        """(row, next position, blocks) of an active sequence (host mirror)."""
+        row, pos, nb = C.c_int32(), C.c_int32(), C.c_int32()
+        check(lib().cottus_decode_batch_sequence(self._h, int(seq_id), C.byref(row), C.byref(pos), None, 0,
+                                                 C.byref(nb)))
+        blocks = (C.c_int32 * max(nb.value, 1))()
+        check(lib().cottus_decode_batch_sequence(self._h, int(seq_id), None, None, blocks, nb.value, None))
+        return row.value, pos.value, [int(blocks[i]) for i in range(nb.value)]
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h:
+            lib().cottus_decode_batch_destroy(h)
             self._h = None

@@ -229,6 +229,61 @@ int cottus_block_allocator_free(cottus_block_allocator *a, int32_t block_id);
 int32_t cottus_block_allocator_num_free(const cottus_block_allocator *a);
 int32_t cottus_block_allocator_total_blocks(const cottus_block_allocator *a);
 
+/* ------------------------------------------------------------------------
+ * host (+ one small kernel per step): batched decode-step driver.  The block
+ * bookkeeping of Engine::generate (engine.cpp:52-95: a block allocated
+ * whenever a sequence's next position starts one, engine.cpp:73-77; blocks
+ * returned in allocation order when the sequence ends, engine.cpp:88-90)
+ * for many sequences at once, with the block table resident in device
+ * memory instead of a host PageTable copied to the device on every call
+ * (paged_attention_cuda.cu:125-135).
+ *
+ * The active sequences occupy rows 0..size-1 of a caller-owned device table
+ * device_block_table[max_batch][max_blocks_per_seq] and of
+ * device_positions[max_batch] (the position of each row's next token).
+ * Adding a sequence appends a row at position 0; releasing one moves the
+ * last row into its place (cottus_decode_batch_rows gives the order).
+ * A step: cottus_decode_batch_begin_step allocates the blocks the step
+ * needs and sends the changed table entries and the positions to the device
+ * (one small kernel on `stream`, parameters passed by value: no device
+ * scratch and no copy call); run cottus_rope_append_decode (or
+ * cottus_rope_append + cottus_paged_decode) once per layer with
+ * batch = cottus_decode_batch_size(), block_table = device_block_table,
+ * positions = device_positions, max_blocks_per_seq as given here; then
+ * cottus_decode_batch_end_step advances every position by one.  With both
+ * device pointers NULL the object keeps the host bookkeeping only.
+ * Errors: COTTUS_ERR_OUT_OF_MEMORY when the pool is exhausted (the step's
+ * allocations are undone; "Out of memory: no free blocks",
+ * block_allocator.cpp:23-25), COTTUS_ERR_OUT_OF_RANGE when a row would pass
+ * max_blocks_per_seq * block_size tokens (the reference's maxSeqLen
+ * length_error, engine.cpp:43-45) or the batch is full.  Not thread-safe.
+ * ---------------------------------------------------------------------- */
+typedef struct cottus_decode_batch cottus_decode_batch;
+typedef struct {
+    int32_t num_blocks;          /* pool capacity in blocks (BlockAllocator totalBlocks) */
+    int32_t block_size;
+    int32_t max_batch;           /* rows of the device table */
+    int32_t max_blocks_per_seq;  /* columns of the device table */
+    int32_t *device_block_table; /* [max_batch][max_blocks_per_seq], or NULL (host bookkeeping only) */
+    int32_t *device_positions;   /* [max_batch], or NULL */
+} cottus_decode_batch_desc;
+
+int cottus_decode_batch_create(const cottus_decode_batch_desc *desc, cottus_decode_batch **out);
+void cottus_decode_batch_destroy(cottus_decode_batch *b);
+/* new sequence at position 0 in the next free row (*row may be NULL) */
+int cottus_decode_batch_add(cottus_decode_batch *b, int64_t seq_id, int32_t *row);
+/* frees the sequence's blocks; the last row moves into its row */
+int cottus_decode_batch_release(cottus_decode_batch *b, int64_t seq_id);
+int cottus_decode_batch_begin_step(cottus_decode_batch *b, cottus_stream_t stream);
+int cottus_decode_batch_end_step(cottus_decode_batch *b);
+int32_t cottus_decode_batch_size(const cottus_decode_batch *b);
+int32_t cottus_decode_batch_free_blocks(const cottus_decode_batch *b);
+/* sequence ids in row order; returns the number of rows */
+int cottus_decode_batch_rows(const cottus_decode_batch *b, int64_t *seq_ids, int32_t cap);
+/* host mirror of one sequence: its row, next position and blocks (up to cap) */
+int cottus_decode_batch_sequence(const cottus_decode_batch *b, int64_t seq_id, int32_t *row, int32_t *position,
+                                 int32_t *blocks, int32_t cap, int32_t *num_blocks);
+
 #ifdef __cplusplus
 }
 #endif

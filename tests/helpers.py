@@ -53,3 +53,48 @@ def max_abs(a, b) -> float:
     a = a.float().cpu().numpy() if isinstance(a, torch.Tensor) else np.asarray(a, np.float32)
     b = b.float().cpu().numpy() if isinstance(b, torch.Tensor) else np.asarray(b, np.float32)
     return float(np.max(np.abs(a.astype(np.float64) - b.astype(np.float64)))) if a.size else 0.0
+
+
+class BatchReplica:
+    """Host model of the batched decode-step driver, built on the oracle's
+    allocator (the restated reference BlockAllocator): Engine::generate's
+    bookkeeping (engine.cpp:52-95) for many sequences, rows in addition
+    order, a released row taken by the last one."""
+
+    def __init__(self, oracle, num_blocks, block_size, max_batch, max_blocks):
+        self.alloc = oracle.allocator(num_blocks, block_size)
+        self.bs, self.max_batch, self.max_blocks = block_size, max_batch, max_blocks
+        self.rows = []   # sequence ids in row order
+        self.seq = {}    # id -> [position, blocks]
+
+    def add(self, sid):
+        self.rows.append(sid)
+        self.seq[sid] = [0, []]
+
+    def release(self, sid):
+        for blk in self.seq[sid][1]:  # allocation order (engine.cpp:88-90)
+            assert self.alloc.free(blk) == 0
+        r = self.rows.index(sid)
+        last = self.rows.pop()
+        if last != sid:
+            self.rows[r] = last
+        del self.seq[sid]
+
+    def begin_step(self):
+        """True if the step's blocks were allocated, False (nothing changed) on exhaustion."""
+        grown = []
+        for sid in self.rows:
+            pos, blocks = self.seq[sid]
+            if pos % self.bs == 0:
+                blk = self.alloc.alloc()
+                if blk < 0:
+                    for g in reversed(grown):
+                        assert self.alloc.free(self.seq[g][1].pop()) == 0
+                    return False
+                blocks.append(blk)
+                grown.append(sid)
+        return True
+
+    def end_step(self):
+        for sid in self.rows:
+            self.seq[sid][0] += 1
