@@ -225,6 +225,8 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="split-context partial exchange: peer memory over NVLink, or NCCL all-gather")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -269,13 +271,22 @@ def main():
     pool_snapshot = t["kv_pool"].clone() if w.fused else None  # the fused step appends; restore is not timed
 
     launches_per_step = 1 if (not split and not w.fused) or w.fused else 2
+    exchange = None
+    if split:
+        from cottus_b200 import parallel
+        if args.exchange == "peer":
+            exchange = parallel.PeerExchange(w.B, w.H, w.D)
 
     def step():
         if w.fused:
             cb.rope_append_decode(t["query"], t["key"], t["value"], t["positions"], t["cos_sin"], t["kv_pool"],
                                   t["block_table"], num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs, out=out)
+        elif split and exchange is not None:
+            # decode kernel (completion flagged to every rank) + combine kernel reading peers over NVLink
+            parallel.split_kv_decode_peer(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], exchange,
+                                          num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
+                                          num_physical_blocks=wl.num_blocks, out_dtype=w.out_dtype, out=out)
         elif split:
-            from cottus_b200 import parallel
             parallel.split_kv_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"],
                                      num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
                                      num_physical_blocks=wl.num_blocks, out_dtype=w.out_dtype, part=part, lse=lse)
@@ -391,6 +402,8 @@ def main():
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {ex}"}
 
+    if exchange is not None:
+        exchange.close()  # collective: every rank is done with the peer buffers
     if world > 1:
         dist.barrier()
     if rank != 0:
@@ -422,13 +435,17 @@ def main():
                    "per_gpu_batch": wl.B, "kv_bytes_per_step_per_gpu": kv_bytes_rank,
                    "l2": ("L2 flushed between steps (2x L2 buffer written)" if small else
                           f"inputs larger than L2 ({kv_bytes_rank / 1e6:.0f} MB KV per GPU vs 126 MB L2), no flush"),
-                   "parallelism": (f"split-KV over {world} GPUs, NCCL all-gather of LSE partials" if split else
+                   "parallelism": ((f"split-KV over {world} GPUs, " +
+                                    ("LSE partials read from peer memory over NVLink after a completion flag raised "
+                                     "by the decode kernel" if exchange is not None else
+                                     "NCCL all-gather of LSE partials")) if split else
                                    f"sequence-sharded over {world} GPU(s), no collective")},
         "tokens_per_s": w.B * (1 if split else world) / (ms * 1e-3),
         "pct_hbm_peak": value / world / peak * 100 if not split else value / world / peak * 100,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": kname + (" + lse_combine_kernel" if split else "") + ": one decode launch per step",
+                     "kernel": kname + ((" + peer_combine_kernel" if exchange is not None else " + lse_combine_kernel")
+                                        if split else "") + ": one decode launch per step",
                      "kernel_ms": kern_ms, "kernel_ms_alone": k_ms, "algorithmic_bytes": alg},
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
     }

@@ -108,6 +108,11 @@ def lib() -> C.CDLL:
         ("cottus_block_allocator_free", C.c_int, [_vp, _i32]),
         ("cottus_block_allocator_num_free", _i32, [_vp]),
         ("cottus_block_allocator_total_blocks", _i32, [_vp]),
+        ("cottus_peer_exchange_create", C.c_int, [_i32, _i32, _i32, _i32, _i32, P(_vp), _vp]),
+        ("cottus_peer_exchange_open", C.c_int, [_vp, _vp]),
+        ("cottus_peer_exchange_destroy", None, [_vp]),
+        ("cottus_split_decode_workspace_size", _sz, [P(PagedDecodeParams)]),
+        ("cottus_split_decode", C.c_int, [P(PagedDecodeParams), _vp, _vp]),
         ("cottus_decode_batch_create", C.c_int, [P(DecodeBatchDesc), P(_vp)]),
         ("cottus_decode_batch_destroy", None, [_vp]),
         ("cottus_decode_batch_add", C.c_int, [_vp, _i64, P(_i32)]),

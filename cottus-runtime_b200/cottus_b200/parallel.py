@@ -5,14 +5,21 @@ its own sequences.  The long-context path splits every sequence's pages
 into contiguous ranges, one per rank; each rank computes normalised partial
 outputs with their log-sum-exp (cottus_paged_decode in partial mode), the
 partials are all-gathered (NCCL over NVLink on GPUs, gloo on CPU), and every
-rank merges them with cottus_lse_combine.
+rank merges them with cottus_lse_combine.  PeerExchange/split_kv_decode_peer
+do the same exchange without a collective library call: partials are read
+from the other ranks' memory over NVLink after a completion flag that the
+decode kernel itself raises (cottus_split_decode).
 """
 from __future__ import annotations
 
+import ctypes as C
+
+import numpy as np
 import torch
 import torch.distributed as dist
 
-from .ops import lse_combine, paged_decode
+from ._lib import check, lib
+from .ops import _stream, lse_combine, make_decode_params, paged_decode, workspace
 
 
 def all_gather_partials(out: torch.Tensor, lse: torch.Tensor, group=None):
@@ -48,3 +55,50 @@ def split_kv_decode(query, kv_pool, block_table, context_lens, *, num_kv_heads, 
                  num_physical_blocks=num_physical_blocks, stream=stream)
     parts, lses = all_gather_partials(part, lse, group)
     return lse_combine(parts, lses, out_dtype=out_dtype, stream=stream)
+
+
+class PeerExchange:
+    """Exchange buffers of a split-context decode, one per rank, mapped by
+    every other rank through CUDA IPC (cottus_peer_exchange_*).  Collective
+    at construction (handles all-gathered over `group`)."""
+
+    def __init__(self, batch: int, num_heads: int, head_dim: int, group=None):
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        handle = (C.c_uint8 * 64)()
+        h = C.c_void_p()
+        check(lib().cottus_peer_exchange_create(world, rank, batch, num_heads, head_dim, C.byref(h), handle))
+        self._h = h
+        dev = torch.device("cuda", torch.cuda.current_device())
+        mine = torch.tensor(bytearray(bytes(handle)), dtype=torch.uint8, device=dev)
+        every = torch.empty(world * 64, dtype=torch.uint8, device=dev)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        blob = np.ascontiguousarray(every.cpu().numpy())
+        check(lib().cottus_peer_exchange_open(self._h, blob.ctypes.data))
+        dist.barrier(group=group)  # every rank mapped every buffer before first use
+        self.group = group
+
+    def close(self):
+        """Collective: every rank stops using the exchange, then frees it."""
+        if self._h:
+            dist.barrier(group=self.group)
+            lib().cottus_peer_exchange_destroy(self._h)
+            self._h = None
+
+
+def split_kv_decode_peer(query, kv_pool, block_table, context_lens, exchange: PeerExchange, *, num_kv_heads,
+                         head_dim, block_size, num_layers=1, layer=0, num_physical_blocks=None,
+                         out_dtype=torch.float16, out=None, lse_out=None, status=None, stream=None):
+    """split_kv_decode with the exchange through peer memory: one decode
+    kernel and one combine kernel per rank, no collective call."""
+    B, H, D = query.shape
+    if out is None:
+        out = torch.empty((B, H, D), dtype=out_dtype, device=query.device)
+    p = make_decode_params(out, query, kv_pool, block_table, context_lens, num_kv_heads=num_kv_heads,
+                           head_dim=head_dim, block_size=block_size, num_layers=num_layers, layer=layer,
+                           num_physical_blocks=num_physical_blocks, lse_out=lse_out, status=status)
+    need = lib().cottus_split_decode_workspace_size(C.byref(p))
+    if need:
+        ws = workspace(need, query.device)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    check(lib().cottus_split_decode(C.byref(p), exchange._h, _stream(stream)))
+    return out

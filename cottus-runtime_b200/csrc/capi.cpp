@@ -180,6 +180,34 @@ int cottus_paged_decode(const cottus_paged_decode_params* p, cottus_stream_t str
     return run_decode(desc_from(p), reinterpret_cast<cudaStream_t>(stream));
 }
 
+}  // extern "C"
+
+namespace cb200 {
+// cottus_paged_decode whose completion is signalled to the ranks of a split
+// context (peer_exchange.cu): by the fast-path kernel itself, or by a
+// signal kernel after the generic one.
+int paged_decode_signalled(const cottus_paged_decode_params* p, const PeerSignal& sig, cudaStream_t st) {
+    if (!p) return fail(COTTUS_ERR_INVALID_ARGUMENT, "params must not be NULL");
+    int rc = check_common(p->batch, p->layer, p->num_heads, p->num_kv_heads, p->head_dim, p->block_size,
+                          p->num_layers, p->max_blocks_per_seq, p->num_physical_blocks);
+    if (rc) return rc;
+    if (!valid_dtype(p->q_dtype) || !valid_dtype(p->out_dtype)) return fail(COTTUS_ERR_INVALID_ARGUMENT, "unknown dtype");
+    if (p->batch <= 0 || !p->out || !p->query || !p->kv_pool || !p->block_table || !p->context_lens)
+        return fail(COTTUS_ERR_INVALID_ARGUMENT, "NULL pointer argument or empty batch");
+    DecodeDesc d = desc_from(p);
+    if (tma_supported(d)) {
+        d.signal = sig;
+        return run_decode(d, st);
+    }
+    rc = run_decode(d, st);
+    if (rc) return rc;
+    const cudaError_t e = launch_peer_signal(sig, st);
+    return e == cudaSuccess ? COTTUS_OK : cuda_fail(e);
+}
+}  // namespace cb200
+
+extern "C" {
+
 int cottus_lse_combine(const cottus_lse_combine_params* p, cottus_stream_t stream) {
     if (!p) return fail(COTTUS_ERR_INVALID_ARGUMENT, "params must not be NULL");
     if (p->num_parts <= 0 || p->batch < 0 || p->num_heads <= 0 || p->head_dim <= 0)

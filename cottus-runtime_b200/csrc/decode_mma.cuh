@@ -93,13 +93,17 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D, G, QSPLIT>())
     int* slot_blk =
         reinterpret_cast<int*>(smem + (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 8) + warp * RING;
 
+    __shared__ unsigned cta_done;  // warps of this CTA that finished (split-context signal)
     if (lane == 0) {
-        if (warp == 0) prefetch_tensormap(&kv_map);
+        if (warp == 0) {
+            prefetch_tensormap(&kv_map);
+            cta_done = 0;
+        }
 #pragma unroll
         for (int r = 0; r < RING; ++r) mbar_init(&bars[r], 1);
         fence_barrier_init();
     }
-    __syncwarp();
+    __syncthreads();
 
     grid_dependency_wait();
     grid_dependents_launch();
@@ -438,6 +442,7 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D, G, QSPLIT>())
         kg += nu;
         cid = NC > W ? grab_chunk(a, W, NC, lane) : NC;
     }
+    signal_done(a, lane, &cta_done);
 }
 
 template <int D, int G, int RING, bool ROPE, bool QSPLIT>

@@ -73,7 +73,34 @@ struct TmaArgs {
     int q_f16, out_f16;
     unsigned epoch;  // per-launch tag of the arrival counters
     float qscale;    // softmax scale * log2(e)
+    PeerSignal sig;  // completion signal to the other ranks of a split context
 };
+
+// End of a warp's work.  In a split-context launch, once every warp of every
+// CTA has stored its outputs, the last one tells every rank that this
+// rank's partials are complete: a system-scope fence, then flag[rank] =
+// epoch in each rank's flag array (peer stores over NVLink).  Each warp's
+// outputs are fenced before it counts itself, so the chain of counts carries
+// all of them before the fence.  A warp that gave up on a wait never counts,
+// and the other ranks' bounded waits report the timeout.
+__device__ __forceinline__ void signal_done(const TmaArgs& a, int lane, unsigned* cta_done) {
+    if (a.sig.world == 0) return;
+    __syncwarp();
+    if (lane == 0) {
+        __threadfence();
+        if (atomicAdd(cta_done, 1u) == kNW - 1) {
+            __threadfence();
+            if (atomicAdd(a.sig.done, 1u) == gridDim.x - 1) {
+                *reinterpret_cast<volatile unsigned*>(a.sig.done) = 0u;  // for the next launch
+                __threadfence_system();
+                for (int r = 0; r < a.sig.world; ++r)
+                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig.flags[r] + a.sig.rank),
+                                 "r"(a.sig.epoch)
+                                 : "memory");
+            }
+        }
+    }
+}
 
 // Pages of sequence b, or 0 when its context is empty or invalid; *ctx_out
 // receives the context length.
@@ -449,13 +476,17 @@ __global__ void __launch_bounds__(kNW * 32)
                                            (size_t)kNW * CH * G * 4 + (size_t)kNW * 2 * G * 4) +
                     warp * RING;
 
+    __shared__ unsigned cta_done;  // warps of this CTA that finished (split-context signal)
     if (lane == 0) {
-        if (warp == 0) prefetch_tensormap(&kv_map);
+        if (warp == 0) {
+            prefetch_tensormap(&kv_map);
+            cta_done = 0;
+        }
 #pragma unroll
         for (int r = 0; r < RING; ++r) mbar_init(&bars[r], 1);
         fence_barrier_init();
     }
-    __syncwarp();
+    __syncthreads();
 
     grid_dependency_wait();
     grid_dependents_launch();
@@ -770,6 +801,7 @@ __global__ void __launch_bounds__(kNW * 32)
         kg += nu;
         cid = NC > W ? grab_chunk(a, W, NC, lane) : NC;
     }
+    signal_done(a, lane, &cta_done);
 }
 
 // ---------------------------------------------------------------------------
@@ -818,6 +850,7 @@ inline TmaArgs make_tma_args(const DecodeDesc& d, long long W, int G, int D) {
     a.ws_ml = a.ws_o + (size_t)2 * max_chunks(W) * G * D;
     a.status = d.status;
     a.epoch = next_epoch();
+    a.sig = d.signal;
     a.k_new = d.k_new;
     a.v_new = d.v_new;
     a.cos_sin = d.cos_sin;

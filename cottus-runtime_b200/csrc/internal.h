@@ -6,7 +6,21 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "cottus_b200.h"
+
 namespace cb200 {
+
+// Completion signal of a split-context decode (one rank of `world`): when
+// the launch has stored all its outputs, its last CTA writes `epoch` to
+// flags[r][rank] for every rank r (device pointers valid on this GPU: its
+// own array, and the peers' mapped over NVLink).  world == 0: none.
+constexpr int kMaxPeers = 8;
+struct PeerSignal {
+    uint32_t* flags[kMaxPeers] = {};
+    uint32_t* done = nullptr;  // CTA completion counter of this launch, zero between launches
+    int32_t rank = 0, world = 0;
+    uint32_t epoch = 0;
+};
 
 // One resolved decode launch.  In rope mode the context length of sequence
 // b is positions[b] + 1 and the kernel first rotates q/k and appends k/v.
@@ -34,6 +48,7 @@ struct DecodeDesc {
     int32_t max_position = 0;
     void* q_out = nullptr;
     uint16_t* kv_mut = nullptr;
+    PeerSignal signal;  // split-context decode across GPUs (fast path kernels)
 };
 
 // Fast path: persistent stream-K TMA kernel (block_size 16, head_dim in
@@ -83,6 +98,12 @@ cudaError_t launch_gather(uint16_t* k_out, uint16_t* v_out, const uint16_t* kv, 
                           const int32_t* context_lens, int64_t num_blocks, int32_t batch, int32_t max_context,
                           int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_layers,
                           int32_t layer, int32_t max_blocks, uint32_t* status, cudaStream_t st);
+
+// Split-context decode (peer_exchange.cu): the decode whose completion is
+// signalled to every rank, and the stand-alone signal used after the
+// generic kernel.
+int paged_decode_signalled(const cottus_paged_decode_params* p, const PeerSignal& sig, cudaStream_t st);
+cudaError_t launch_peer_signal(const PeerSignal& sig, cudaStream_t st);
 
 // Host-side (cos, sin) of the reference formula (compute_primitives_cpu.cpp:54-57).
 void rope_cos_sin_host(int32_t pos, int32_t pair, int32_t head_dim, float theta, float* c, float* s);

@@ -1,0 +1,263 @@
+// Split-context decode across the GPUs of one node without a collective
+// library call: the exchange of partial results goes through peer memory
+// over NVLink.
+//
+// Each rank owns one exchange buffer (cudaMalloc'd once, mapped by every
+// other rank through CUDA IPC): a flag per rank, the decode's CTA counter,
+// and two slots of partials ([batch][heads][head_dim] normalised fp32
+// outputs and [batch][heads] natural-log LSEs).  A step on every rank:
+//   1. the decode kernel writes this rank's partials into its own slot
+//      (epoch & 1) and, when its last CTA has finished, stores `epoch` into
+//      flag[rank] of every rank's buffer (decode_tma.cuh: signal_done);
+//   2. the combine kernel waits (bounded) until every rank's flag in its own
+//      buffer reads `epoch`, then reads every rank's slot directly (peer
+//      loads) and merges them, the arithmetic of cottus_lse_combine.
+// Two slots suffice: a rank overwrites slot s at step n+2 only after its
+// combine of step n+1, which waited for every rank's step-n+1 decode, which
+// each rank started after its own combine of step n had read slot s.
+// Plain loads and stores only (no bulk or tensor copies of peer memory).
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "cottus_b200.h"
+#include "internal.h"
+
+namespace cb200 {
+int set_error(int code, const std::string& msg);
+
+namespace {
+
+constexpr size_t kAlign = 256;
+constexpr long long kPeerWaitCycles = 2000000000LL;  // about a second at 2 GHz
+
+size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
+
+struct Layout {
+    size_t flags, done, slot0, slot_bytes, part_bytes, total;
+};
+
+Layout layout_of(int world, long long heads, int head_dim) {
+    Layout l;
+    l.flags = 0;
+    l.done = align_up(sizeof(uint32_t) * kMaxPeers);
+    l.slot0 = l.done + kAlign;
+    l.part_bytes = align_up((size_t)heads * head_dim * sizeof(float));
+    l.slot_bytes = l.part_bytes + align_up((size_t)heads * sizeof(float));
+    l.total = l.slot0 + 2 * l.slot_bytes;
+    (void)world;
+    return l;
+}
+
+struct PeerSlots {
+    const float* part[kMaxPeers];
+    const float* lse[kMaxPeers];
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// One warp per (sequence, head); lanes over head_dim.  Same operations, in
+// the same order, as lse_combine_kernel over parts 0..world-1.
+__global__ void peer_combine_kernel(const __grid_constant__ PeerSlots src, int world, const uint32_t* flags,
+                                    uint32_t epoch, void* out, int out_f16, float* lse_out, long long heads, int D,
+                                    uint32_t* status) {
+    __shared__ int ready;
+    grid_dependency_wait();    // this rank's decode has completed (its own flag is then set as well)
+    grid_dependents_launch();  // the next decode may start its prologue while this merge runs
+    if (threadIdx.x == 0) {
+        bool ok = true;
+        const long long t0 = clock64();
+        for (int r = 0; r < world && ok; ++r)
+            while (ld_acquire_sys(flags + r) != epoch)
+                if (clock64() - t0 > kPeerWaitCycles) {
+                    ok = false;
+                    break;
+                }
+        ready = ok;
+        if (!ok && blockIdx.x == 0) report(status, COTTUS_STATUS_TIMEOUT);
+    }
+    __syncthreads();
+    if (!ready) return;
+    const long long hw = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (hw >= heads) return;
+    float M = -INFINITY;
+    for (int p = 0; p < world; ++p) M = fmaxf(M, src.lse[p][hw]);
+    float S = 0.f;
+    if (M != -INFINITY)
+        for (int p = 0; p < world; ++p) S += expf(src.lse[p][hw] - M);
+    const float lse = M == -INFINITY ? -INFINITY : M + logf(S);
+    for (int d = lane; d < D; d += 32) {
+        float acc = 0.f;
+        if (M != -INFINITY)
+            for (int p = 0; p < world; ++p) {
+                const float lp = src.lse[p][hw];
+                if (lp != -INFINITY) acc += expf(lp - lse) * src.part[p][hw * D + d];
+            }
+        if (out_f16) reinterpret_cast<__half*>(out)[hw * D + d] = __float2half_rn(acc);
+        else reinterpret_cast<float*>(out)[hw * D + d] = acc;
+    }
+    if (lse_out && lane == 0) lse_out[hw] = lse;
+}
+
+__global__ void peer_signal_kernel(PeerSignal sig) {
+    __threadfence_system();
+    for (int r = 0; r < sig.world; ++r)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(sig.flags[r] + sig.rank), "r"(sig.epoch) : "memory");
+}
+
+}  // namespace
+
+cudaError_t launch_peer_signal(const PeerSignal& sig, cudaStream_t st) {
+    peer_signal_kernel<<<1, 1, 0, st>>>(sig);
+    return cudaGetLastError();
+}
+}  // namespace cb200
+
+struct cottus_peer_exchange {
+    int world = 0, rank = 0, batch = 0, heads = 0, head_dim = 0;
+    cb200::Layout lay{};
+    uint8_t* local = nullptr;                 // this rank's buffer
+    uint8_t* base[cb200::kMaxPeers] = {};     // every rank's buffer as seen from this GPU
+    bool opened = false;
+    uint32_t epoch = 0;
+};
+
+namespace {
+
+int fail(int code, const std::string& msg) { return cb200::set_error(code, msg); }
+int cuda_fail(cudaError_t e) { return fail(COTTUS_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(e)); }
+
+}  // namespace
+
+extern "C" {
+
+int cottus_peer_exchange_create(int32_t world, int32_t rank, int32_t batch, int32_t num_heads, int32_t head_dim,
+                                cottus_peer_exchange** out, void* ipc_handle) {
+    if (!out || !ipc_handle) return fail(COTTUS_ERR_INVALID_ARGUMENT, "NULL argument");
+    *out = nullptr;
+    if (world < 1 || world > cb200::kMaxPeers || rank < 0 || rank >= world)
+        return fail(COTTUS_ERR_INVALID_ARGUMENT, "world must be in [1, 8] and rank in [0, world)");
+    if (batch <= 0 || num_heads <= 0 || head_dim <= 0 || head_dim > 512)
+        return fail(COTTUS_ERR_INVALID_ARGUMENT, "batch, num_heads and head_dim must be positive (head_dim <= 512)");
+    auto* ex = new cottus_peer_exchange;
+    ex->world = world;
+    ex->rank = rank;
+    ex->batch = batch;
+    ex->heads = num_heads;
+    ex->head_dim = head_dim;
+    ex->lay = cb200::layout_of(world, (long long)batch * num_heads, head_dim);
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, ex->lay.total);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, ex->lay.total);
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+    if (e != cudaSuccess) {
+        if (p) cudaFree(p);
+        delete ex;
+        return cuda_fail(e);
+    }
+    static_assert(sizeof(cudaIpcMemHandle_t) == COTTUS_IPC_HANDLE_BYTES, "IPC handle size");
+    std::memcpy(ipc_handle, &h, sizeof h);
+    ex->local = static_cast<uint8_t*>(p);
+    ex->base[rank] = ex->local;
+    *out = ex;
+    return COTTUS_OK;
+}
+
+int cottus_peer_exchange_open(cottus_peer_exchange* ex, const void* handles) {
+    if (!ex || !handles) return fail(COTTUS_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (ex->opened) return fail(COTTUS_ERR_INVALID_ARGUMENT, "exchange already opened");
+    const auto* hs = static_cast<const uint8_t*>(handles);
+    for (int r = 0; r < ex->world; ++r) {
+        if (r == ex->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, hs + (size_t)r * COTTUS_IPC_HANDLE_BYTES, sizeof h);
+        void* p = nullptr;
+        const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; ++q)
+                if (q != ex->rank && ex->base[q]) {
+                    cudaIpcCloseMemHandle(ex->base[q]);
+                    ex->base[q] = nullptr;
+                }
+            return cuda_fail(e);
+        }
+        ex->base[r] = static_cast<uint8_t*>(p);
+    }
+    ex->opened = true;
+    return COTTUS_OK;
+}
+
+void cottus_peer_exchange_destroy(cottus_peer_exchange* ex) {
+    if (!ex) return;
+    for (int r = 0; r < ex->world; ++r)
+        if (r != ex->rank && ex->base[r]) cudaIpcCloseMemHandle(ex->base[r]);
+    if (ex->local) cudaFree(ex->local);
+    delete ex;
+}
+
+size_t cottus_split_decode_workspace_size(const cottus_paged_decode_params* p) {
+    if (!p) return 0;
+    cottus_paged_decode_params q = *p;  // the decode runs in partial mode: fp32 outputs and LSEs
+    float dummy;
+    q.out_dtype = COTTUS_F32;
+    q.lse_out = &dummy;
+    return cottus_paged_decode_workspace_size(&q);
+}
+
+int cottus_split_decode(const cottus_paged_decode_params* p, cottus_peer_exchange* ex, cottus_stream_t stream) {
+    if (!p || !ex) return fail(COTTUS_ERR_INVALID_ARGUMENT, "NULL argument");
+    if (!ex->opened) return fail(COTTUS_ERR_INVALID_ARGUMENT, "exchange not opened (cottus_peer_exchange_open)");
+    if (p->batch != ex->batch || p->num_heads != ex->heads || p->head_dim != ex->head_dim)
+        return fail(COTTUS_ERR_INVALID_ARGUMENT, "batch, num_heads and head_dim must match the exchange");
+    if (p->out_dtype != COTTUS_F32 && p->out_dtype != COTTUS_F16)
+        return fail(COTTUS_ERR_INVALID_ARGUMENT, "unsupported dtype");
+    const uint32_t epoch = ++ex->epoch;
+    const size_t slot = ex->lay.slot0 + (size_t)(epoch & 1u) * ex->lay.slot_bytes;
+    // 1. this rank's partials into its own slot, completion flagged to every rank
+    cottus_paged_decode_params q = *p;
+    q.out = ex->local + slot;
+    q.out_dtype = COTTUS_F32;
+    q.lse_out = reinterpret_cast<float*>(ex->local + slot + ex->lay.part_bytes);
+    cb200::PeerSignal sig;
+    for (int r = 0; r < ex->world; ++r) sig.flags[r] = reinterpret_cast<uint32_t*>(ex->base[r] + ex->lay.flags);
+    sig.done = reinterpret_cast<uint32_t*>(ex->local + ex->lay.done);
+    sig.rank = ex->rank;
+    sig.world = ex->world;
+    sig.epoch = epoch;
+    const int rc = cb200::paged_decode_signalled(&q, sig, reinterpret_cast<cudaStream_t>(stream));
+    if (rc != COTTUS_OK) return rc;
+    // 2. wait for every rank's flag, pull and merge
+    cb200::PeerSlots src;
+    for (int r = 0; r < ex->world; ++r) {
+        src.part[r] = reinterpret_cast<const float*>(ex->base[r] + slot);
+        src.lse[r] = reinterpret_cast<const float*>(ex->base[r] + slot + ex->lay.part_bytes);
+    }
+    const long long heads = (long long)ex->batch * ex->heads;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((heads * 32 + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, cb200::peer_combine_kernel, src, ex->world,
+                                             reinterpret_cast<const uint32_t*>(ex->local + ex->lay.flags), epoch,
+                                             p->out, (int)(p->out_dtype == COTTUS_F16), p->lse_out, heads,
+                                             ex->head_dim, p->status);
+    if (e != cudaSuccess) return cuda_fail(e);
+    return COTTUS_OK;
+}
+
+}  // extern "C"

@@ -284,6 +284,39 @@ int cottus_decode_batch_rows(const cottus_decode_batch *b, int64_t *seq_ids, int
 int cottus_decode_batch_sequence(const cottus_decode_batch *b, int64_t seq_id, int32_t *row, int32_t *position,
                                  int32_t *blocks, int32_t cap, int32_t *num_blocks);
 
+/* ------------------------------------------------------------------------
+ * Split-context decode across the GPUs of one node, exchange through peer
+ * memory (no collective library call).  No reference counterpart (the
+ * reference never splits a context); the merged result equals the
+ * un-split cottus::pagedAttentionCUDA output.
+ *
+ * Every rank (one process per GPU) creates an exchange for its
+ * (batch, num_heads, head_dim) — one cudaMalloc at set-up, nothing per
+ * call — gives its 64-byte IPC handle to every other rank (any host
+ * transport), opens all handles, and then calls cottus_split_decode in
+ * lockstep with the other ranks: p describes this rank's page range of
+ * every sequence (its pool shard, block table and token counts); p->out
+ * receives the merged output [batch][num_heads][head_dim] and p->lse_out
+ * (optional) the merged natural-log LSE.  One decode kernel (partials into
+ * this rank's exchange buffer, completion flagged to every rank by its last
+ * CTA) and one combine kernel (bounded wait for every rank's flag, then
+ * peer loads over NVLink and the merge of cottus_lse_combine).  A rank that
+ * does not take part makes the others' combine give up after about a
+ * second with COTTUS_STATUS_TIMEOUT in p->status.  At most 8 ranks.
+ * ---------------------------------------------------------------------- */
+#define COTTUS_IPC_HANDLE_BYTES 64
+typedef struct cottus_peer_exchange cottus_peer_exchange;
+int cottus_peer_exchange_create(int32_t world, int32_t rank, int32_t batch, int32_t num_heads, int32_t head_dim,
+                                cottus_peer_exchange **out, void *ipc_handle /* COTTUS_IPC_HANDLE_BYTES, out */);
+/* handles: world x COTTUS_IPC_HANDLE_BYTES, in rank order (this rank's own is skipped) */
+int cottus_peer_exchange_open(cottus_peer_exchange *ex, const void *handles);
+/* call on every rank only after all ranks stopped using the exchange */
+void cottus_peer_exchange_destroy(cottus_peer_exchange *ex);
+/* p->workspace must hold cottus_split_decode_workspace_size(p) bytes (the
+ * decode runs in partial mode), under the rules of cottus_paged_decode. */
+size_t cottus_split_decode_workspace_size(const cottus_paged_decode_params *p);
+int cottus_split_decode(const cottus_paged_decode_params *p, cottus_peer_exchange *ex, cottus_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

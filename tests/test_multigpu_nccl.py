@@ -1,6 +1,7 @@
-"""Split-KV decode across GPUs over NCCL (needs two or more GPUs): each rank
-holds a contiguous page range of every sequence; the merged output must
-match the un-split kernel within the fp16 bound on every rank."""
+"""Split-KV decode across GPUs (needs two or more GPUs): each rank holds a
+contiguous page range of every sequence; the merged output must match the
+un-split kernel within the fp16 bound on every rank, over NCCL and, bit for
+bit the same, through peer memory (cottus_split_decode)."""
 import json
 import socket
 import subprocess
@@ -38,3 +39,5 @@ def test_split_kv_over_nccl(tmp_path, world):
     v = json.loads(out.read_text())
     assert v["ranks_agree"]
     assert v["max_abs"] <= TOL_F16
+    assert v["peer_equal_all_ranks"]
+    assert v["peer_status"] == [0] * world
