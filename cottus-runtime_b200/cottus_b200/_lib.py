@@ -68,6 +68,17 @@ class DecodeBatchDesc(C.Structure):
     ]
 
 
+class QkvParams(C.Structure):
+    _fields_ = [
+        ("x", _vp), ("weight", _vp), ("hidden", _i32), ("positions", _vp), ("cos_sin", _vp), ("max_position", _i32),
+        ("kv_pool", _vp), ("block_table", _vp), ("num_physical_blocks", _i64),
+        ("batch", _i32), ("num_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32), ("block_size", _i32),
+        ("num_layers", _i32), ("layer", _i32), ("max_blocks_per_seq", _i32),
+        ("query_out", _vp), ("query_out_dtype", _i32), ("qkv_out", _vp),
+        ("workspace", _vp), ("workspace_bytes", _sz), ("status", _vp),
+    ]
+
+
 class CottusError(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"{message} (code {code})")
@@ -108,6 +119,8 @@ def lib() -> C.CDLL:
         ("cottus_block_allocator_free", C.c_int, [_vp, _i32]),
         ("cottus_block_allocator_num_free", _i32, [_vp]),
         ("cottus_block_allocator_total_blocks", _i32, [_vp]),
+        ("cottus_qkv_rope_append_workspace_size", _sz, [P(QkvParams)]),
+        ("cottus_qkv_rope_append", C.c_int, [P(QkvParams), _vp]),
         ("cottus_peer_exchange_create", C.c_int, [_i32, _i32, _i32, _i32, _i32, P(_vp), _vp]),
         ("cottus_peer_exchange_open", C.c_int, [_vp, _vp]),
         ("cottus_peer_exchange_destroy", None, [_vp]),

@@ -11,8 +11,8 @@ import ctypes as C
 import torch
 
 from . import _lib
-from ._lib import (F16, F32, CottusError, DecodeBatchDesc, DecodeStepParams, LseCombineParams, PagedDecodeParams, check,
-                   lib)
+from ._lib import (F16, F32, CottusError, DecodeBatchDesc, DecodeStepParams, LseCombineParams, PagedDecodeParams,
+                   QkvParams, check, lib)
 
 _DT = {torch.float32: F32, torch.float16: F16}
 
@@ -198,6 +198,35 @@ def rope_append_decode(query, key, value, positions, cos_sin, kv_pool, block_tab
         p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
     check(lib().cottus_rope_append_decode(C.byref(p), _stream(stream)))
     return out
+
+
+def qkv_rope_append(x, weight, positions, cos_sin, kv_pool, block_table, *, num_heads, num_kv_heads, head_dim,
+                    block_size, num_layers=1, layer=0, num_physical_blocks=None, query_out=None,
+                    query_out_dtype=torch.float16, qkv_out=None, status=None, stream=None):
+    """QKV projection + RoPE + KV append in one kernel (cottus_qkv_rope_append).
+    x [B][hidden] fp16, weight [(H + 2 Hkv) D][hidden] fp16; returns the rotated query."""
+    for t, n in ((x, "x"), (weight, "weight"), (kv_pool, "kv_pool")):
+        _require(t, n)
+    B, hidden = x.shape
+    if num_physical_blocks is None:
+        num_physical_blocks = kv_pool.numel() // (2 * num_layers * block_size * num_kv_heads * head_dim)
+    if query_out is None:
+        query_out = torch.empty((B, num_heads, head_dim), dtype=query_out_dtype, device=x.device)
+    p = QkvParams()
+    p.x, p.weight, p.hidden = x.data_ptr(), weight.data_ptr(), hidden
+    p.positions, p.cos_sin, p.max_position = positions.data_ptr(), cos_sin.data_ptr(), cos_sin.shape[0]
+    p.kv_pool, p.block_table, p.num_physical_blocks = kv_pool.data_ptr(), block_table.data_ptr(), int(num_physical_blocks)
+    p.batch, p.num_heads, p.num_kv_heads, p.head_dim = B, num_heads, num_kv_heads, head_dim
+    p.block_size, p.num_layers, p.layer, p.max_blocks_per_seq = block_size, num_layers, layer, block_table.shape[1]
+    p.query_out, p.query_out_dtype = query_out.data_ptr(), _dtype_code(query_out)
+    p.qkv_out = qkv_out.data_ptr() if qkv_out is not None else None
+    p.status = status.data_ptr() if status is not None else None
+    need = lib().cottus_qkv_rope_append_workspace_size(C.byref(p))
+    if need:
+        ws = workspace(need, x.device)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    check(lib().cottus_qkv_rope_append(C.byref(p), _stream(stream)))
+    return query_out
 
 
 def paged_gather(kv_pool, block_table, context_lens, *, max_context, num_kv_heads, head_dim, block_size,

@@ -82,6 +82,28 @@ CUtensorMap make_kv_tensor_map(const DecodeDesc& d, bool swizzle128, cudaError_t
     return map;
 }
 
+// 2-D tiled map over a row-major fp16 matrix [outer][inner] (row pitch
+// `pitch_bytes`), box {box_inner, box_outer}, optionally 128-byte swizzled.
+CUtensorMap make_tensor_map_2d_f16(const void* base, uint64_t inner, uint64_t outer, uint64_t pitch_bytes,
+                                   uint32_t box_inner, uint32_t box_outer, bool swizzle128, cudaError_t* err) {
+    CUtensorMap map;
+    std::memset(&map, 0, sizeof map);
+    auto fn = encode_fn();
+    if (!fn) {
+        *err = cudaErrorNotSupported;
+        return map;
+    }
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)pitch_bytes};
+    cuuint32_t box[2] = {box_inner, box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    *err = r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+    return map;
+}
+
 // Leading bytes of a decode workspace: the chunk queue word and one arrival
 // counter per (sequence, kv head) pair, rounded to 256 bytes.
 size_t workspace_zero_prefix_bytes(int32_t batch, int32_t num_kv_heads) {

@@ -204,6 +204,52 @@ size_t cottus_rope_append_decode_workspace_size(const cottus_decode_step_params 
 int cottus_rope_append_decode(const cottus_decode_step_params *p, cottus_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * The step before attention, fused: QKV projection of each sequence's new
+ * token, RoPE on q and k, and the KV append, in one kernel.  Replaces
+ * generic_transformer.cpp:169-284 per layer and token (gemmCUDA x3 =
+ * cuBLAS SGEMM, compute_primitives_cuda.cu:30-55; ropeCUDA x2; the host
+ * truncating encode and scatter).  Weights and activations are fp16 with
+ * fp32 accumulation:  qkv[b][n] = sum_k x[b][k] * weight[n][k], rows n of
+ * `weight` = Wq rows (num_heads*head_dim), then Wk, then Wv rows (the
+ * reference's [hidden][out] matrices transposed and stacked).  Then, as
+ * cottus_rope_append: q and k rotated at positions[b] with the (cos, sin)
+ * table, the rotated query written to query_out, k and v encoded by
+ * truncation into slot positions[b] % block_size of block
+ * block_table[b][positions[b] / block_size], layer `layer`.  hidden and the
+ * stacked row count must be multiples of 64; batches above 64 run as
+ * several launches.  Feed query_out to cottus_paged_decode with
+ * context_lens = positions + 1 for the attention.
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const void *x;              /* [batch][hidden] fp16, 16-B aligned */
+    const void *weight;         /* [(num_heads + 2*num_kv_heads)*head_dim][hidden] fp16, 16-B aligned */
+    int32_t hidden;
+    const int32_t *positions;   /* [batch] */
+    const float *cos_sin;       /* device [max_position][head_dim/2][2] (cottus_rope_cos_sin_fill) */
+    int32_t max_position;
+    uint16_t *kv_pool;
+    const int32_t *block_table; /* [batch][max_blocks_per_seq] */
+    int64_t num_physical_blocks;
+    int32_t batch;
+    int32_t num_heads;
+    int32_t num_kv_heads;
+    int32_t head_dim;
+    int32_t block_size;
+    int32_t num_layers;
+    int32_t layer;
+    int32_t max_blocks_per_seq;
+    void *query_out;            /* [batch][num_heads][head_dim] rotated query */
+    int32_t query_out_dtype;    /* enum cottus_dtype */
+    float *qkv_out;             /* optional [batch][rows] fp32 projections before rotation */
+    void *workspace;            /* cottus_qkv_rope_append_workspace_size() bytes, 16-B aligned, any contents */
+    size_t workspace_bytes;
+    uint32_t *status;           /* optional device word */
+} cottus_qkv_params;
+
+size_t cottus_qkv_rope_append_workspace_size(const cottus_qkv_params *p);
+int cottus_qkv_rope_append(const cottus_qkv_params *p, cottus_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Block-table gather: copies, bit for bit, the K and V rows of layer
  * `layer` for the first context_lens[b] tokens of each sequence into dense
  * k_out/v_out [batch][max_context][num_kv_heads][head_dim] (fp16 bits);

@@ -140,6 +140,18 @@ int oracle_paged_attention_batch(float *out, const float *query, const uint16_t 
     return ORACLE_OK;
 }
 
+/* compute_primitives_cpu.cpp:6-23 (gemmCPU): C[m][n] = sum over k, in
+ * increasing k, of A[m][k] * B[k][n], each product rounded to float and
+ * added in float (the file is compiled without contraction). */
+void oracle_gemm(float *c, const float *a, const float *b, int32_t m, int32_t n, int32_t k) {
+    for (int32_t i = 0; i < m; ++i)
+        for (int32_t j = 0; j < n; ++j) {
+            float sum = 0.0f;
+            for (int32_t t = 0; t < k; ++t) sum += a[(size_t)i * k + t] * b[(size_t)t * n + j];
+            c[(size_t)i * n + j] = sum;
+        }
+}
+
 void oracle_rope_cos_sin(int32_t pos, int32_t pair, int32_t head_dim, float theta, float *cos_out,
                          float *sin_out) {
     /* compute_primitives_cpu.cpp:54-57: float pow/cos/sin of float arguments */

@@ -72,6 +72,7 @@ void oracle_rope(float *out, const float *in, int32_t pos, int32_t num_heads, in
 
 /* cos/sin of the RoPE angle for one (pos, pair), evaluated with the same
  * float expressions as compute_primitives_cpu.cpp:54-57. */
+void oracle_gemm(float *c, const float *a, const float *b, int32_t m, int32_t n, int32_t k);
 void oracle_rope_cos_sin(int32_t pos, int32_t pair, int32_t head_dim, float theta, float *cos_out,
                          float *sin_out);
 

@@ -60,6 +60,7 @@ class Oracle:
         _sig(L.oracle_paged_attention_batch, C.c_int, _f32p, _f32p, C.c_void_p, _i32p, _i32, _i32p,
              _i32, _i32, _i32, _i32, _i32, _i32, _i32)
         _sig(L.oracle_rope, None, _f32p, _f32p, _i32, _i32, _i32, _f32)
+        _sig(L.oracle_gemm, None, _f32p, _f32p, _f32p, _i32, _i32, _i32)
         _sig(L.oracle_rope_cos_sin, None, _i32, _i32, _i32, _f32, C.POINTER(_f32), C.POINTER(_f32))
         _sig(L.oracle_kv_append, C.c_int, _u16p, _f32p, _f32p, _i32p, _i32, _i32, _i32, _i32, _i32,
              _i32, _i32)
@@ -137,6 +138,14 @@ class Oracle:
         self.lib.oracle_rope(out, x, pos, num_heads, head_dim, theta)
         return out
 
+    def gemm(self, a, b):
+        """gemmCPU restated: a [M][K] @ b [K][N] in float, k increasing."""
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        c = np.empty((a.shape[0], b.shape[1]), np.float32)
+        self.lib.oracle_gemm(c, a, b, a.shape[0], b.shape[1], a.shape[1])
+        return c
+
     def rope_cos_sin(self, pos, pair, head_dim, theta=10000.0):
         c, s = _f32(), _f32()
         self.lib.oracle_rope_cos_sin(pos, pair, head_dim, theta, C.byref(c), C.byref(s))
@@ -205,6 +214,7 @@ class Reference:
         _sig(L.ref_paged_attention_cpu_batch, C.c_int, _f32p, _f32p, C.POINTER(C.c_void_p), _i32p, _i32,
              _i32p, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _i32)
         _sig(L.ref_rope_cpu, None, _f32p, _f32p, _i32, _i32, _i32, _f32)
+        _sig(L.ref_gemm_cpu, None, _f32p, _f32p, _f32p, _i32, _i32, _i32)
         _sig(L.ref_allocator_create, C.c_void_p, _i32, _i32)
         _sig(L.ref_allocator_destroy, None, C.c_void_p)
         _sig(L.ref_allocator_alloc, _i32, C.c_void_p)
@@ -243,6 +253,13 @@ class Reference:
         out = np.empty_like(x)
         self.lib.ref_rope_cpu(out, x, pos, num_heads, head_dim, theta)
         return out
+
+    def gemm(self, a, b):
+        a = np.ascontiguousarray(a, np.float32)
+        b = np.ascontiguousarray(b, np.float32)
+        c = np.empty((a.shape[0], b.shape[1]), np.float32)
+        self.lib.ref_gemm_cpu(c, a, b, a.shape[0], b.shape[1], a.shape[1])
+        return c
 
     def allocator(self, total_blocks, block_size):
         return _Alloc(self.lib, "ref_allocator", total_blocks, block_size)

@@ -83,6 +83,11 @@ int ref_paged_attention_cpu_batch(float *out, const float *query, const void *co
 }
 
 // cottus::ropeCPU (compute_primitives_cpu.cpp:46-73).
+// cottus::gemmCPU (compute_primitives_cpu.cpp:6-23): C[M][N] = A[M][K] B[K][N].
+void ref_gemm_cpu(float *c, const float *a, const float *b, int32_t m, int32_t n, int32_t k) {
+    cottus::gemmCPU(c, a, b, m, n, k);
+}
+
 void ref_rope_cpu(float *out, const float *in, int32_t pos, int32_t num_heads, int32_t head_dim,
                   float theta) {
     cottus::ropeCPU(out, in, pos, num_heads, head_dim, theta);

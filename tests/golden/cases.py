@@ -140,6 +140,19 @@ def rope_cases():
 
 # -- allocator churn --------------------------------------------------------------
 
+def gemm_cases():
+    """Inputs of gemmCPU (compute_primitives_cpu.cpp:6-23) golden vectors:
+    decode-shaped products (one to a few tokens x a projection), fp16-valued
+    operands stored as float, as the fused QKV step uses them."""
+    rng = np.random.default_rng(401)
+    out = {}
+    for name, (m, k, n) in {"m1": (1, 256, 192), "m5": (5, 128, 320)}.items():
+        a = fp16_bits_to_f32(fp32_to_fp16_trunc(rng.standard_normal((m, k), dtype=np.float32)))
+        b = fp16_bits_to_f32(fp32_to_fp16_trunc(rng.standard_normal((k, n), dtype=np.float32) / np.float32(16)))
+        out[name] = (a.reshape(m, k), b.reshape(k, n))
+    return out
+
+
 def allocator_ops(seed=301, n_ops=10000, total=512):
     """Seeded alloc/free op list: +1 = alloc, -k-1 = free the k-th live block."""
     rng = np.random.default_rng(seed)

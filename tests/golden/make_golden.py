@@ -6,8 +6,8 @@ engine` into oracle/_ref/):
     python tests/golden/make_golden.py
 
 Everything stored comes out of the reference library (paged attention,
-RoPE, block allocator, page-table bounds, and the KV cache written by
-GenericTransformer::forwardToken); inputs are regenerated from cases.py and
+RoPE, gemmCPU, block allocator, page-table bounds, and the KV cache written
+by GenericTransformer::forwardToken); inputs are regenerated from cases.py and
 only their SHA-256 is stored.
 """
 from __future__ import annotations
@@ -90,6 +90,10 @@ def main():
                                          for p in r["positions"]])
     out["rope/x64_out"] = np.stack([ref.rope(r["x64"], int(p), 4, 64) for p in r["positions"]])
     meta["rope"] = dict(input_sha=cases.sha(r["positions"], r["kat_in"], r["x64"]))
+
+    for name, (a, b) in cases.gemm_cases().items():
+        out[f"gemm/{name}"] = ref.gemm(a, b)
+        meta[f"gemm/{name}"] = dict(input_sha=cases.sha(a, b))
 
     ops, total = cases.allocator_ops()
     a = ref.allocator(total, 16)

@@ -62,6 +62,14 @@ def test_rope_bit_exact(oracle, golden):
         np.testing.assert_array_equal(cs, golden["rope/cos_sin_d128"][i])
 
 
+@pytest.mark.parametrize("name", sorted(cases.gemm_cases()))
+def test_gemm_bit_exact(oracle, golden, name):
+    """gemmCPU restated (the fused QKV projection's oracle) against the reference's own."""
+    a, b = cases.gemm_cases()[name]
+    assert cases.sha(a, b) == MANIFEST[f"gemm/{name}"]["input_sha"]
+    np.testing.assert_array_equal(oracle.gemm(a, b).view(np.uint32), golden[f"gemm/{name}"].view(np.uint32))
+
+
 def test_allocator_trace(oracle, golden):
     ops, total = cases.allocator_ops()
     a = oracle.allocator(total, 16)
