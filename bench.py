@@ -174,6 +174,25 @@ def run_reference(args, rank, world):
     import torch
     if world > 1 and rank != 0:
         return
+    if args.config == "qkv_llama3_8b":
+        budget = min(2.0, 60.0 / max(args.steps + args.warmup, 1))
+        rates, sample, threads = [], "", 1
+        t0 = time.perf_counter()
+        for i in range(args.warmup + args.steps):
+            r, threads, sample = qkv_reference_rate(target_s=budget)
+            if i >= args.warmup:
+                rates.append(r)
+        v = float(np.mean(rates))
+        print(json.dumps({"metric": "fused QKV+RoPE+append tokens/s", "value": v, "unit": "tokens/s", "n_gpus": world,
+                          "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": (time.perf_counter() - t0) / max(args.steps + args.warmup, 1) * 1e3,
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                          "data": "synthetic", "config": {"workload": "qkv_llama3_8b"}, "impl": "reference",
+                          "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                                           "sample": sample},
+                          "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return
     from cottus_b200 import workloads as W
     w = build_workload(args.config, 0, args.batch)
     t = W.device_tensors(w, "cpu" if not torch.cuda.is_available() else "cuda")
@@ -214,6 +233,160 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+QKV = dict(hidden=4096, H=32, Hkv=8, D=128, B=64, layers=4, bs=16, maxb=128)  # Llama-3-8B projection, batch 64
+
+
+def qkv_inputs(dev, seed=7):
+    import torch
+    q = QKV
+    N = (q["H"] + 2 * q["Hkv"]) * q["D"]
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = (torch.randn((q["B"], q["hidden"]), generator=g)).half()
+    ws = [(torch.randn((N, q["hidden"]), generator=g) / q["hidden"] ** 0.5).half() for _ in range(q["layers"])]
+    nb = q["B"] * q["maxb"]
+    table = torch.randperm(nb, generator=g).int().view(q["B"], q["maxb"])
+    pos = torch.randint(0, q["maxb"] * q["bs"], (q["B"],), generator=g).int()
+    return N, x, ws, table, pos, nb
+
+
+def run_qkv(args, rank, world, local):
+    """The fused QKV projection + RoPE + KV append (cottus_qkv_rope_append) on
+    the Llama-3-8B projection (hidden 4096 -> 6144 rows), batch 64; each step
+    one layer, cycling over 4 layers' weights (201 MB > L2) as a decode step
+    does.  Replicas per GPU (weak scaling, no collective)."""
+    import torch
+    import torch.distributed as dist
+    import cottus_b200 as cb
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    q = QKV
+    N, x, ws, table, pos, nb = qkv_inputs(dev)
+    x, table, pos = x.to(dev), table.to(dev), pos.to(dev)
+    ws = [w.to(dev) for w in ws]
+    tab = cb.rope_cos_sin_table(q["maxb"] * q["bs"], q["D"]).to(dev)
+    pool = torch.zeros(nb * 2 * q["layers"] * q["bs"] * q["Hkv"] * q["D"], dtype=torch.int16, device=dev)
+    qout = torch.empty((q["B"], q["H"], q["D"]), dtype=torch.float16, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    kw = dict(num_heads=q["H"], num_kv_heads=q["Hkv"], head_dim=q["D"], block_size=q["bs"], num_layers=q["layers"],
+              num_physical_blocks=nb, query_out=qout)
+
+    def step(i, xx=x):
+        cb.qkv_rope_append(xx, ws[i % q["layers"]], pos, tab, pool, table, layer=i % q["layers"], **kw)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    # end to end: the step's activations from pinned host memory, the rotated query back
+    hx = x.cpu().pin_memory()
+    hq = torch.empty(qout.shape, dtype=qout.dtype).pin_memory()
+    dx = torch.empty_like(x)
+    n_e2e = max(min(args.steps // 5, 2000), 10)
+    for i in range(3):
+        dx.copy_(hx, non_blocking=True)
+        step(i, dx)
+        hq.copy_(qout, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(n_e2e):
+        dx.copy_(hx, non_blocking=True)
+        step(i, dx)
+        hq.copy_(qout, non_blocking=True)
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    e_ms = a.elapsed_time(b) / n_e2e
+    if world > 1:
+        tt = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_ms = float(tt.item())
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r, cores, sample = qkv_reference_rate(target_s=6.0)
+        cpu = {"value": r, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample}
+    if world > 1:
+        dist.barrier()
+        if rank != 0:
+            dist.destroy_process_group()
+            return
+    peak, peak_kind = peaks()
+    wbytes = N * q["hidden"] * 2
+    alg = wbytes + x.numel() * 2 + qout.numel() * 2 + q["B"] * 2 * q["Hkv"] * q["D"] * 2 + q["B"] * 8
+    line = {
+        "metric": "fused QKV+RoPE+append tokens/s", "value": world * q["B"] / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 x f16 -> f32",
+        "data": "synthetic: seeded N(0,1) activations, N(0, 1/hidden) fp16 weights",
+        "config": {"workload": f"qkv_llama3_8b: hidden {q['hidden']} -> {N} rows (H{q['H']}/Hkv{q['Hkv']}/D{q['D']}), "
+                               f"batch {q['B']}, one of {q['layers']} layers per step",
+                   "l2": f"{q['layers']} layers' weights ({q['layers'] * wbytes / 1e6:.0f} MB) cycled, > 126 MB L2",
+                   "parallelism": f"replicas on {world} GPU(s), no collective"},
+        "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": alg / (ms * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "qkv_proj_kernel: one launch per step", "kernel_ms": ms, "algorithmic_bytes": alg},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * q["B"] / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 2,
+                "d2h_bytes_per_step": qout.numel() * 2, "ms_per_step": e_ms,
+                "api": "cottus_qkv_rope_append (C ABI via ctypes)"},
+        "gpu_launches": args.steps, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def qkv_reference_rate(target_s=6.0, tokens=None):
+    """The reference's CPU step for one token and one layer (gemmCPU x3 as one
+    stacked product, ropeCPU on q and k; fp32 weights as the reference keeps
+    them), tokens spread over the host threads; returns (tokens/s, threads, sample)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle.oracle import Reference
+
+    q = QKV
+    ref = Reference()
+    N = (q["H"] + 2 * q["Hkv"]) * q["D"]
+    rng = np.random.default_rng(3)
+    wt = (rng.standard_normal((q["hidden"], N), dtype=np.float32) / np.float32(q["hidden"] ** 0.5))
+    threads = os.cpu_count() or 1
+    n_tok = tokens or threads
+    xs = rng.standard_normal((n_tok, q["hidden"]), dtype=np.float32)
+
+    def one(i):
+        out = ref.gemm(xs[i:i + 1], wt)
+        ref.rope(out[0, :q["H"] * q["D"]], 5, q["H"], q["D"])
+        ref.rope(out[0, q["H"] * q["D"]:(q["H"] + q["Hkv"]) * q["D"]], 5, q["Hkv"], q["D"])
+
+    done, t0 = 0, time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        while True:
+            list(ex.map(one, range(n_tok)))
+            done += n_tok
+            el = time.perf_counter() - t0
+            if el >= target_s:
+                break
+    return done / el, threads, f"{done} tokens x 1 layer ({el:.1f} s wall, {threads} threads)"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -221,7 +394,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=50)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="llama3_8b",
-                    choices=["tinyllama_f32", "llama3_8b", "ragged_mha", "long_ctx_70b", "fused_tinyllama"])
+                    choices=["tinyllama_f32", "llama3_8b", "ragged_mha", "long_ctx_70b", "fused_tinyllama",
+                             "qkv_llama3_8b"])
     ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -239,6 +413,9 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.config == "qkv_llama3_8b":
+        run_qkv(args, rank, world, local)
         return
 
     import cottus_b200 as cb

@@ -9,19 +9,27 @@
 // out[t][n] = sum_k x[t][k] * W[n][k] for the batch's tokens t (at most 64
 // per launch, more are chunked by the host) and the stacked rows n of Wq,
 // Wk, Wv.  The op streams the weights once, so HBM bandwidth bounds it:
-//   * CTA tile: 64 weight rows x all tokens, a split of the K range; grid =
-//     (rows/64) x splits, splits chosen so the grid covers the SMs twice;
+//   * CTA tile: 128 weight rows x all tokens (padded to 16, 32 or 64), a
+//     split of the K range; grid = (rows/128) x splits, splits chosen so the
+//     grid fits in one wave of two CTAs per SM;
 //   * weights and activations staged by TMA in 64-element (128-byte) rows
-//     with 128B swizzle through a 6-stage mbarrier ring (one producer
-//     thread, per-stage full/empty barriers);
-//   * each warp multiplies 16 weight rows by all tokens on the tensor cores
-//     (mma.sync m16n8k16, fp16 in, fp32 accumulate; A = weights by ldmatrix,
-//     B = activations by ldmatrix, both from the swizzled tiles);
-//   * split partial sums go to the workspace; the last CTA of a row tile to
-//     finish (epoch-tagged counter) adds them in split order (deterministic),
-//     rotates q and k with the (cos, sin) table of the reference formula
-//     (FMA-free, bit-identical to ropeCPU on the same sums), writes the
-//     rotated query, and encodes k and v by truncation into the pool.
+//     with 128B swizzle through an 8-stage mbarrier ring (warp 0 produces;
+//     up to 192 KB in flight, one CTA per SM);
+//   * 5th-generation tensor cores: one thread of warp 1 issues
+//     tcgen05.mma (kind::f16, M = 128 weight rows, N = tokens, K = 16, fp32
+//     accumulator in tensor memory) straight from the swizzled tiles
+//     through shared-memory matrix descriptors, and tcgen05.commit frees
+//     each stage when its multiplies are done; the four warps then read the
+//     accumulator rows of their 32 TMEM lanes with tcgen05.ld;
+//   * the splits of one row tile form a thread-block cluster: each CTA puts
+//     its partial sums in its own shared memory, and after a cluster
+//     barrier every CTA finishes a share of the tile's (token, row pair)
+//     items, reading the partials of all CTAs of the cluster through
+//     distributed shared memory and adding them in split order
+//     (deterministic); then it rotates q and k with the (cos, sin) table of
+//     the reference formula (FMA-free, bit-identical to ropeCPU on the same
+//     sums), writes the rotated query, and encodes k and v by truncation
+//     into the pool.  No global workspace, no atomics.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -39,9 +47,9 @@ CUtensorMap make_tensor_map_2d_f16(const void* base, uint64_t inner, uint64_t ou
 
 namespace {
 
-constexpr int kQRows = 64;   // weight rows per CTA tile
+constexpr int kQRows = 128;  // weight rows per CTA tile (the MMA's M)
 constexpr int kQK = 64;      // k elements per stage (one 128-byte swizzled row)
-constexpr int kQStages = 6;  // ring depth
+constexpr int kQStages = 8;  // ring depth: 8 stages of weights + activations in flight per CTA (one CTA per SM)
 constexpr int kQThreads = 128;
 constexpr int kQMaxTokens = 64;
 
@@ -56,30 +64,68 @@ struct QkvArgs {
     void* q_out;
     int q_out_f16;
     float* qkv_out;
-    float* part;                    // [splits][B][N]
-    unsigned long long* counters;   // [row tiles]
-    unsigned epoch;
     int splits, ksteps, ks_per_split;
     uint32_t* status;
 };
 
 template <int BP>
 constexpr size_t qkv_smem_bytes() {
-    return (size_t)kQStages * (kQRows * kQK * 2 + BP * kQK * 2) + 2 * kQStages * 8 + 1024;
+    return (size_t)kQStages * (kQRows * kQK * 2 + BP * kQK * 2) + (2 * kQStages + 1) * 8 + 1024;
+}
+
+// Shared-memory matrix descriptor of a K-major tile written by TMA with
+// 128B swizzle (rows of 128 bytes, 8-row groups 1024 bytes apart; the tile
+// base 1024-byte aligned): start address >> 4, leading offset 1 (unused
+// when swizzled), stride offset 1024 >> 4, descriptor version 1, layout
+// SWIZZLE_128B (2).  A k-slice of 16 elements starts 32 bytes further.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t smem_byte_addr) {
+    return (uint64_t)((smem_byte_addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor of kind::f16: fp16 A and B, fp32 accumulator,
+// both K-major, N = tokens, M = 128.
+template <int N>
+constexpr uint32_t f16_idesc() {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kQRows >> 4) << 24);
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Thread-block cluster: barrier over all threads of all CTAs, rank, and
+// loads from another CTA's shared memory.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t map_cluster(uint32_t local_smem_addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ float2 ld_cluster_f2(uint32_t cluster_addr) {
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(cluster_addr) : "memory");
+    return v;
 }
 
 template <int BP>
 __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_constant__ CUtensorMap wmap,
                                                               const __grid_constant__ CUtensorMap xmap,
                                                               const QkvArgs a) {
-    constexpr unsigned FULL = 0xffffffffu;
     constexpr int W_BYTES = kQRows * kQK * 2, X_BYTES = BP * kQK * 2, STAGE = W_BYTES + X_BYTES;
-    constexpr int NT = BP / 8;  // token tiles of 8
+    constexpr uint32_t TMEM_COLS = BP < 32 ? 32 : BP;
+    static_assert(STAGE % 1024 == 0, "stages must keep 1024-byte alignment for the 128B swizzle");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)kQStages * STAGE);
     uint64_t* empty = full + kQStages;
-    __shared__ int last_tile;
+    uint64_t* done = empty + kQStages;
+    __shared__ uint32_t tmem_base;
+    __shared__ int failed, issued, consumed;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile = blockIdx.x, split = blockIdx.y;
     const int row0 = tile * kQRows;
@@ -92,171 +138,224 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
         prefetch_tensormap(&xmap);
         for (int s = 0; s < kQStages; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kQThreads / 32);
+            mbar_init(&empty[s], 1);
         }
+        mbar_init(done, 1);
         fence_barrier_init();
+        failed = 0;
+        issued = consumed = 0;
     }
+    if (warp == 0) {  // accumulator: TMEM_COLS columns x 128 lanes
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
     grid_dependency_wait();
     grid_dependents_launch();
 
-    auto issue = [&](int i) {  // thread 0: stage i of this split
-        const int slot = i % kQStages;
-        uint8_t* st = smem + (size_t)slot * STAGE;
-        mbar_arrive_expect_tx(&full[slot], STAGE);
-        const int kx = (k0 + i) * kQK;
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-                smem_addr(st)),
-            "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(kx), "r"(row0), "r"(smem_addr(&full[slot]))
-            : "memory");
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-                smem_addr(st + W_BYTES)),
-            "l"(reinterpret_cast<uint64_t>(&xmap)), "r"(kx), "r"(0), "r"(smem_addr(&full[slot]))
-            : "memory");
-    };
-    if (threadIdx.x == 0)
-        for (int i = 0; i < nsteps && i < kQStages; ++i) issue(i);
-
-    float acc[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-
-    bool ok = true;
-    int consumed = 0;
-    for (int i = 0; i < nsteps; ++i) {
-        const int slot = i % kQStages;
-        ok = __all_sync(FULL, mbar_wait_bounded(&full[slot], (i / kQStages) & 1));
-        if (!ok) break;
-        const uint32_t ws = smem_addr(smem + (size_t)slot * STAGE), xs = ws + W_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < kQK / 16; ++kk) {
-            uint32_t af[4];
-            {
-                const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                ldsm_x4(ws + swz(0, row, kk * 2 + (lane >> 4)), af);
-            }
-#pragma unroll
-            for (int jp = 0; jp < NT / 2; ++jp) {
-                uint32_t bf[4];
-                const int tok = jp * 16 + (lane & 7) + ((lane >> 4) << 3);
-                ldsm_x4(xs + swz(0, tok, kk * 2 + ((lane >> 3) & 1)), bf);
-                mma16816(acc[2 * jp], af, bf[0], bf[1]);
-                mma16816(acc[2 * jp + 1], af, bf[2], bf[3]);
-            }
-        }
-        __syncwarp();
-        consumed = i + 1;
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        if (threadIdx.x == 0 && i + kQStages < nsteps) {
-            // the slot is free once every warp has read it
-            ok = mbar_wait_bounded(&empty[slot], (i / kQStages) & 1);
-            if (ok) {
-                fence_proxy_async_smem();
-                issue(i + kQStages);
-            }
-        }
-        ok = __all_sync(FULL, ok);
-        if (!ok) break;
-    }
-    if (!__syncthreads_and(ok)) {
-        if (threadIdx.x == 0) {
-            report(a.status, COTTUS_STATUS_TIMEOUT);
-            // let the copies still in flight land (bounded) before the CTA leaves
-            const int issued = min(nsteps, consumed + kQStages);
-            for (int i = consumed; i < issued; ++i) (void)mbar_wait_bounded(&full[i % kQStages], (i / kQStages) & 1);
-        }
-        return;
-    }
-
-    // ---- split partials: C fragment rows are weight rows, columns tokens ----
-    {
-        const int r = row0 + warp * 16 + (lane >> 2);
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-            const int t = j * 8 + (lane & 3) * 2;
-            float* p = a.part + (size_t)split * a.B * a.N;
-            if (t < a.B) {
-                p[(size_t)t * a.N + r] = acc[j][0];
-                p[(size_t)t * a.N + r + 8] = acc[j][2];
-            }
-            if (t + 1 < a.B) {
-                p[(size_t)(t + 1) * a.N + r] = acc[j][1];
-                p[(size_t)(t + 1) * a.N + r + 8] = acc[j][3];
-            }
-        }
-    }
-    // ---- the last split of this row tile finishes it ------------------------
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int last = 1;
-        if (a.splits > 1) {
-            unsigned long long* ctr = a.counters + tile;
-            unsigned long long old = 0;
-            while (true) {  // each failure means another split arrived: at most `splits` rounds
-                const unsigned long long nv =
-                    (unsigned)(old >> 32) == a.epoch ? old + 1 : (((unsigned long long)a.epoch << 32) | 1ull);
-                const unsigned long long prev = atomicCAS(ctr, old, nv);
-                if (prev == old) {
-                    last = (int)(nv & 0xffffffffull) == a.splits;
-                    break;
-                }
-                old = prev;
-            }
-            if (last) __threadfence();
-        }
-        last_tile = last;
-    }
-    __syncthreads();
-    if (!last_tile) return;
-
+    // ---- this CTA's share of the tile's (token, row pair) items, and the
+    // position, (cos, sin) and block id each needs, loaded now so that the
+    // loads overlap the main loop ------------------------------------------------
+    constexpr int EI = 8;  // items per thread whose inputs are held in registers
     const int pairs = kQRows / 2;
     const int HD = a.H * a.D, KD = a.Hkv * a.D;
-    for (int idx = threadIdx.x; idx < a.B * pairs; idx += kQThreads) {
-        const int t = idx / pairs, n = row0 + 2 * (idx % pairs);
-        float v0 = 0.f, v1 = 0.f;
-        for (int s = 0; s < a.splits; ++s) {
-            const float2 pv = __ldcg(reinterpret_cast<const float2*>(a.part + ((size_t)s * a.B + t) * a.N + n));
-            v0 = __fadd_rn(v0, pv.x);
-            v1 = __fadd_rn(v1, pv.y);
+    const int items = a.B * pairs;
+    const int rank = (int)cluster_rank();
+    const int i0 = (int)((long long)items * rank / a.splits), i1 = (int)((long long)items * (rank + 1) / a.splits);
+    int mpos[EI], mblk[EI];
+    float2 mcs[EI];
+    auto load_meta = [&](int base) {
+#pragma unroll
+        for (int k = 0; k < EI; ++k) {
+            const int idx = base + k * kQThreads;
+            mpos[k] = -1;
+            mblk[k] = -1;
+            mcs[k] = make_float2(0.f, 0.f);
+            if (idx >= i1) continue;
+            const int t = idx / pairs, n = row0 + 2 * (idx % pairs);
+            const int p = a.pos[t];
+            if (p < 0 || p >= a.max_pos || p >= a.maxb * a.bs) continue;
+            mpos[k] = p;
+            if (n < HD + KD)
+                mcs[k] = *reinterpret_cast<const float2*>(a.cos_sin + ((size_t)p * (a.D / 2) + (n % a.D) / 2) * 2);
+            if (n >= HD) mblk[k] = a.bt[(size_t)t * a.maxb + p / a.bs];
         }
-        if (a.qkv_out) *reinterpret_cast<float2*>(a.qkv_out + (size_t)t * a.N + n) = make_float2(v0, v1);
-        const int p = a.pos[t];
-        if (p < 0 || p >= a.max_pos || p >= a.maxb * a.bs) {
-            if ((idx % pairs) == 0) report(a.status, COTTUS_STATUS_BAD_POSITION);
-            continue;
-        }
-        const int d = n % a.D;
-        if (n < HD + KD) {  // q or k: rotate the interleaved pair (d, d + 1)
-            const float2 cs = *reinterpret_cast<const float2*>(a.cos_sin + ((size_t)p * (a.D / 2) + d / 2) * 2);
-            rope_pair(v0, v1, cs.x, cs.y, v0, v1);
-        }
-        if (n < HD) {
-            const size_t e = (size_t)t * HD + n;
-            if (a.q_out_f16) {
-                reinterpret_cast<__half*>(a.q_out)[e] = __float2half_rn(v0);
-                reinterpret_cast<__half*>(a.q_out)[e + 1] = __float2half_rn(v1);
-            } else {
-                reinterpret_cast<float*>(a.q_out)[e] = v0;
-                reinterpret_cast<float*>(a.q_out)[e + 1] = v1;
+    };
+    const bool has_role = threadIdx.x == 0 || threadIdx.x == 32;  // the producer and the MMA issuer start at once
+    if (!has_role) load_meta(i0 + (int)threadIdx.x);
+
+    if (threadIdx.x == 0) {
+        // ---- producer: weights and activations of stage i ----------------
+        for (int i = 0; i < nsteps; ++i) {
+            const int slot = i % kQStages;
+            if (i >= kQStages && !mbar_wait_bounded(&empty[slot], ((i / kQStages) - 1) & 1)) {
+                failed = 1;
+                break;
             }
-            continue;
+            uint8_t* st = smem + (size_t)slot * STAGE;
+            mbar_arrive_expect_tx(&full[slot], STAGE);
+            const int kx = (k0 + i) * kQK;
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                    smem_addr(st)),
+                "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(kx), "r"(row0), "r"(smem_addr(&full[slot]))
+                : "memory");
+            asm volatile(
+                "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                    smem_addr(st + W_BYTES)),
+                "l"(reinterpret_cast<uint64_t>(&xmap)), "r"(kx), "r"(0), "r"(smem_addr(&full[slot]))
+                : "memory");
+            issued = i + 1;
         }
-        const bool is_v = n >= HD + KD;
-        const int kvh = (n - HD - (is_v ? KD : 0)) / a.D;
-        const int blk = a.bt[(size_t)t * a.maxb + p / a.bs];
-        if (blk < 0 || (long long)blk >= a.num_blocks) {
-            if ((idx % pairs) == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
-            continue;
+    } else if (threadIdx.x == 32) {
+        // ---- MMA issue: D[128 rows][BP tokens] += W[rows][k] . X[tokens][k]^T
+        constexpr uint32_t idesc = f16_idesc<BP>();
+        for (int i = 0; i < nsteps; ++i) {
+            const int slot = i % kQStages;
+            if (!mbar_wait_bounded(&full[slot], (i / kQStages) & 1)) {
+                failed = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t wa = smem_addr(smem + (size_t)slot * STAGE), xa = wa + W_BYTES;
+#pragma unroll
+            for (int kk = 0; kk < kQK / 16; ++kk) {
+                const uint64_t ad = sw128_desc(wa + kk * 32), bd = sw128_desc(xa + kk * 32);
+                const uint32_t accumulate = (i | kk) != 0;
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(tmem),
+                    "l"(ad), "l"(bd), "r"(idesc), "r"(accumulate), "r"(0u)
+                    : "memory");
+            }
+            // the stage is free once these multiplies have read it
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_addr(&empty[slot]))
+                         : "memory");
+            consumed = i + 1;
         }
-        // [block][layer][K|V][slot][kv head][dim] (generic_transformer.cpp:234-281)
-        const size_t off = ((((size_t)blk * a.L + a.layer) * 2 + (is_v ? 1 : 0)) * a.bs + (p % a.bs)) * KD +
-                           (size_t)kvh * a.D + d;
-        a.kv[off] = f32_to_f16_trunc(v0);
-        a.kv[off + 1] = f32_to_f16_trunc(v1);
+        // every multiply issued so far is complete when `done` fires
+        if (consumed > 0)
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_addr(done))
+                         : "memory");
+        else
+            mbar_arrive(done);
     }
+    if (has_role) load_meta(i0 + (int)threadIdx.x);
+    __syncwarp();
+    const bool got = mbar_wait_bounded(done, 0);
+    tc_fence_after();
+    const bool ok = __syncthreads_and(got) && !failed;
+    if (!ok && threadIdx.x == 0) {
+        // the other CTAs of the cluster still count on this one: report, let the
+        // copies still in flight land (bounded), and go on with zero partials
+        report(a.status, COTTUS_STATUS_TIMEOUT);
+        for (int i = consumed; i < issued; ++i) (void)mbar_wait_bounded(&full[i % kQStages], (i / kQStages) & 1);
+    }
+    __syncthreads();
+
+    // ---- this split's partials into shared memory: red[token][row] ----------
+    // (the stage buffers are free: every multiply has completed)
+    float* red = reinterpret_cast<float*>(smem);
+    {
+        const int r = warp * 32 + lane;
+#pragma unroll
+        for (int c0 = 0; c0 < BP; c0 += 16) {
+            uint32_t v[16];
+            if (nsteps > 0 && ok) {
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                      "=r"(v[15])
+                    : "r"(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            } else {
+#pragma unroll
+                for (int j = 0; j < 16; ++j) v[j] = 0u;  // an empty (or failed) split contributes zeros
+            }
+#pragma unroll
+            for (int j = 0; j < 16; ++j) red[(c0 + j) * kQRows + r] = __uint_as_float(v[j]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    cluster_sync();  // every split's partials are in place
+
+    // ---- finish this CTA's items: sum the splits, rotate, store ----------------
+    const uint32_t red_local = smem_addr(red);
+    for (int base = i0 + (int)threadIdx.x, chunk = 0; base < i1; base += EI * kQThreads, ++chunk) {
+        if (chunk > 0) load_meta(base);
+        // the EI items' partial sums from every split, one split at a time with
+        // the EI loads in flight together, added in split order
+        float2 sum[EI];
+#pragma unroll
+        for (int k = 0; k < EI; ++k) sum[k] = make_float2(0.f, 0.f);
+        for (int s2 = 0; s2 < a.splits; ++s2) {
+            float2 pv[EI];
+#pragma unroll
+            for (int k = 0; k < EI; ++k) {
+                const int idx = base + k * kQThreads;
+                const int t = idx / pairs, n = row0 + 2 * (idx % pairs);
+                pv[k] = idx < i1 ? ld_cluster_f2(map_cluster(red_local + (uint32_t)((t * kQRows + (n - row0)) * 4),
+                                                             (uint32_t)s2))
+                                 : make_float2(0.f, 0.f);
+            }
+#pragma unroll
+            for (int k = 0; k < EI; ++k) {
+                sum[k].x = __fadd_rn(sum[k].x, pv[k].x);
+                sum[k].y = __fadd_rn(sum[k].y, pv[k].y);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < EI; ++k) {
+            const int idx = base + k * kQThreads;
+            if (idx >= i1) break;
+            const int t = idx / pairs, n = row0 + 2 * (idx % pairs);
+            float v0 = sum[k].x, v1 = sum[k].y;
+            if (a.qkv_out) *reinterpret_cast<float2*>(a.qkv_out + (size_t)t * a.N + n) = make_float2(v0, v1);
+            const int p = mpos[k];
+            if (p < 0) {
+                if ((idx % pairs) == 0) report(a.status, COTTUS_STATUS_BAD_POSITION);
+                continue;
+            }
+            const int d = n % a.D;
+            if (n < HD + KD) rope_pair(v0, v1, mcs[k].x, mcs[k].y, v0, v1);  // q or k: the pair (d, d + 1)
+            if (n < HD) {
+                const size_t e = (size_t)t * HD + n;
+                if (a.q_out_f16) {
+                    reinterpret_cast<__half*>(a.q_out)[e] = __float2half_rn(v0);
+                    reinterpret_cast<__half*>(a.q_out)[e + 1] = __float2half_rn(v1);
+                } else {
+                    reinterpret_cast<float*>(a.q_out)[e] = v0;
+                    reinterpret_cast<float*>(a.q_out)[e + 1] = v1;
+                }
+                continue;
+            }
+            const bool is_v = n >= HD + KD;
+            const int kvh = (n - HD - (is_v ? KD : 0)) / a.D;
+            const int blk = mblk[k];
+            if (blk < 0 || (long long)blk >= a.num_blocks) {
+                if ((idx % pairs) == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
+                continue;
+            }
+            // [block][layer][K|V][slot][kv head][dim] (generic_transformer.cpp:234-281)
+            const size_t o = ((((size_t)blk * a.L + a.layer) * 2 + (is_v ? 1 : 0)) * a.bs + (p % a.bs)) * KD +
+                             (size_t)kvh * a.D + d;
+            a.kv[o] = f32_to_f16_trunc(v0);
+            a.kv[o + 1] = f32_to_f16_trunc(v1);
+        }
+    }
+    cluster_sync();  // no CTA leaves while others may still read its partials
 }
 
 template <int BP>
@@ -276,41 +375,68 @@ cudaError_t launch_qkv(const CUtensorMap& wmap, const CUtensorMap& xmap, const Q
     cfg.blockDim = dim3(kQThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;  // the splits of a row tile
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = a.splits;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     return cudaLaunchKernelEx(&cfg, kern, wmap, xmap, a);
 }
 
-int splits_for(int row_tiles, int ksteps, int sms) {
-    int s = (2 * sms + row_tiles - 1) / row_tiles;
-    if (s < 1) s = 1;
-    if (s > ksteps) s = ksteps;
-    return s;
+// Splits of K: one cluster of `splits` CTAs per row tile (at most 8, the
+// portable cluster size), as many as still let every cluster of the grid be
+// resident at once (clusters are placed whole inside a GPC, so that count
+// comes from the occupancy API rather than from SMs x CTAs per SM).
+template <int BP>
+int splits_for(int row_tiles, int ksteps) {
+    static int cache[64][9] = {};  // [device][splits] -> max active clusters (+1)
+    int dev = 0;
+    cudaGetDevice(&dev);
+    auto kern = qkv_proj_kernel<BP>;
+    const size_t smem = qkv_smem_bytes<BP>();
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    for (int s = (ksteps < 8 ? ksteps : 8); s > 1; --s) {
+        int active = 0;
+        if (dev >= 0 && dev < 64 && cache[dev][s]) {
+            active = cache[dev][s] - 1;
+        } else {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(row_tiles, s);
+            cfg.blockDim = dim3(kQThreads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 1;
+            attr[0].val.clusterDim.y = s;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess) {
+                (void)cudaGetLastError();
+                active = 0;
+            }
+            if (dev >= 0 && dev < 64) cache[dev][s] = active + 1;
+        }
+        if (active >= row_tiles) return s;
+    }
+    return 1;
 }
 
 int fail(int code, const std::string& msg) { return set_error(code, msg); }
 
 }  // namespace
 
-int device_sm_count(int device);
-unsigned next_epoch();
-
 }  // namespace cb200
 
 extern "C" {
 
 size_t cottus_qkv_rope_append_workspace_size(const cottus_qkv_params* p) {
-    if (!p || p->batch <= 0 || p->hidden <= 0 || p->head_dim <= 0) return 0;
-    const long long N = (long long)(p->num_heads + 2 * p->num_kv_heads) * p->head_dim;
-    const int row_tiles = (int)(N / cb200::kQRows), ksteps = p->hidden / cb200::kQK;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int S = cb200::splits_for(row_tiles > 0 ? row_tiles : 1, ksteps > 0 ? ksteps : 1, cb200::device_sm_count(dev));
-    const long long B = p->batch < cb200::kQMaxTokens ? p->batch : cb200::kQMaxTokens;
-    return (((size_t)row_tiles * 8 + 255) & ~size_t(255)) + (size_t)S * B * N * sizeof(float);
+    (void)p;
+    return 0;  // split partials stay in the shared memory of each row tile's cluster
 }
 
 int cottus_qkv_rope_append(const cottus_qkv_params* p, cottus_stream_t stream) {
@@ -323,7 +449,7 @@ int cottus_qkv_rope_append(const cottus_qkv_params* p, cottus_stream_t stream) {
     if (p->batch == 0) return COTTUS_OK;
     const long long N = (long long)(p->num_heads + 2 * p->num_kv_heads) * p->head_dim;
     if (p->hidden % kQK != 0 || N % kQRows != 0 || (p->head_dim % 2) != 0)
-        return fail(COTTUS_ERR_UNSUPPORTED, "hidden must be a multiple of 64, the stacked q/k/v rows a multiple of 64, "
+        return fail(COTTUS_ERR_UNSUPPORTED, "hidden must be a multiple of 64, the stacked q/k/v rows a multiple of 128, "
                                             "and head_dim even");
     if (N >= (1LL << 31) / 2) return fail(COTTUS_ERR_UNSUPPORTED, "projection too large");
     if (!p->x || !p->weight || !p->positions || !p->cos_sin || !p->kv_pool || !p->block_table || !p->query_out)
@@ -332,15 +458,8 @@ int cottus_qkv_rope_append(const cottus_qkv_params* p, cottus_stream_t stream) {
         return fail(COTTUS_ERR_INVALID_ARGUMENT, "x and weight must be 16-byte aligned");
     if (p->query_out_dtype != COTTUS_F16 && p->query_out_dtype != COTTUS_F32)
         return fail(COTTUS_ERR_INVALID_ARGUMENT, "unknown dtype");
-    const size_t need = cottus_qkv_rope_append_workspace_size(p);
-    if (!p->workspace || p->workspace_bytes < need || (reinterpret_cast<uintptr_t>(p->workspace) & 15))
-        return fail(COTTUS_ERR_WORKSPACE, "workspace missing, unaligned or smaller than the required " +
-                                              std::to_string(need) + " bytes");
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int row_tiles = (int)(N / kQRows), ksteps = p->hidden / kQK;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    const int S = splits_for(row_tiles, ksteps, device_sm_count(dev));
     cudaError_t err = cudaSuccess;
     const CUtensorMap wmap = make_tensor_map_2d_f16(p->weight, p->hidden, N, (uint64_t)p->hidden * 2, kQK, kQRows,
                                                     true, &err);
@@ -373,9 +492,8 @@ int cottus_qkv_rope_append(const cottus_qkv_params* p, cottus_stream_t stream) {
         a.q_out = static_cast<uint8_t*>(p->query_out) + (size_t)b0 * p->num_heads * p->head_dim * qe;
         a.q_out_f16 = p->query_out_dtype == COTTUS_F16;
         a.qkv_out = p->qkv_out ? p->qkv_out + (size_t)b0 * N : nullptr;
-        a.counters = static_cast<unsigned long long*>(p->workspace);
-        a.part = reinterpret_cast<float*>(static_cast<uint8_t*>(p->workspace) + (((size_t)row_tiles * 8 + 255) & ~size_t(255)));
-        a.epoch = next_epoch();
+        const int S = BP == 16 ? splits_for<16>(row_tiles, ksteps)
+                               : (BP == 32 ? splits_for<32>(row_tiles, ksteps) : splits_for<64>(row_tiles, ksteps));
         a.splits = S;
         a.ksteps = ksteps;
         a.ks_per_split = (ksteps + S - 1) / S;

@@ -215,8 +215,8 @@ int cottus_rope_append_decode(const cottus_decode_step_params *p, cottus_stream_
  * cottus_rope_append: q and k rotated at positions[b] with the (cos, sin)
  * table, the rotated query written to query_out, k and v encoded by
  * truncation into slot positions[b] % block_size of block
- * block_table[b][positions[b] / block_size], layer `layer`.  hidden and the
- * stacked row count must be multiples of 64; batches above 64 run as
+ * block_table[b][positions[b] / block_size], layer `layer`.  hidden must be
+ * a multiple of 64 and the stacked row count of 128; batches above 64 run as
  * several launches.  Feed query_out to cottus_paged_decode with
  * context_lens = positions + 1 for the attention.
  * ---------------------------------------------------------------------- */
@@ -241,7 +241,7 @@ typedef struct {
     void *query_out;            /* [batch][num_heads][head_dim] rotated query */
     int32_t query_out_dtype;    /* enum cottus_dtype */
     float *qkv_out;             /* optional [batch][rows] fp32 projections before rotation */
-    void *workspace;            /* cottus_qkv_rope_append_workspace_size() bytes, 16-B aligned, any contents */
+    void *workspace;            /* unused: cottus_qkv_rope_append_workspace_size() is 0 */
     size_t workspace_bytes;
     uint32_t *status;           /* optional device word */
 } cottus_qkv_params;
