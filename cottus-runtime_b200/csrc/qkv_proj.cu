@@ -13,23 +13,20 @@
 //     split of the K range; grid = (rows/128) x splits, splits chosen so the
 //     grid fits in one wave of two CTAs per SM;
 //   * weights and activations staged by TMA in 64-element (128-byte) rows
-//     with 128B swizzle through an 8-stage mbarrier ring (warp 0 produces;
-//     up to 192 KB in flight, one CTA per SM);
+//     with 128B swizzle through a 4-stage mbarrier ring (warp 0 produces;
+//     two CTAs per SM);
 //   * 5th-generation tensor cores: one thread of warp 1 issues
 //     tcgen05.mma (kind::f16, M = 128 weight rows, N = tokens, K = 16, fp32
 //     accumulator in tensor memory) straight from the swizzled tiles
 //     through shared-memory matrix descriptors, and tcgen05.commit frees
 //     each stage when its multiplies are done; the four warps then read the
 //     accumulator rows of their 32 TMEM lanes with tcgen05.ld;
-//   * the splits of one row tile form a thread-block cluster: each CTA puts
-//     its partial sums in its own shared memory, and after a cluster
-//     barrier every CTA finishes a share of the tile's (token, row pair)
-//     items, reading the partials of all CTAs of the cluster through
-//     distributed shared memory and adding them in split order
-//     (deterministic); then it rotates q and k with the (cos, sin) table of
-//     the reference formula (FMA-free, bit-identical to ropeCPU on the same
-//     sums), writes the rotated query, and encodes k and v by truncation
-//     into the pool.  No global workspace, no atomics.
+//   * each split writes its partial sums to the workspace; a second kernel
+//     (programmatic dependent launch, one thread per (token, row pair))
+//     adds the splits in order (deterministic), rotates q and k with the
+//     (cos, sin) table of the reference formula (FMA-free, bit-identical to
+//     ropeCPU on the same sums), writes the rotated query, and encodes k and
+//     v by truncation into the pool.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -49,7 +46,7 @@ namespace {
 
 constexpr int kQRows = 128;  // weight rows per CTA tile (the MMA's M)
 constexpr int kQK = 64;      // k elements per stage (one 128-byte swizzled row)
-constexpr int kQStages = 8;  // ring depth: 8 stages of weights + activations in flight per CTA (one CTA per SM)
+constexpr int kQStages = 4;  // ring depth (two CTAs per SM)
 constexpr int kQThreads = 128;
 constexpr int kQMaxTokens = 64;
 
@@ -64,6 +61,7 @@ struct QkvArgs {
     void* q_out;
     int q_out_f16;
     float* qkv_out;
+    float* part;  // [splits][B][N]
     int splits, ksteps, ks_per_split;
     uint32_t* status;
 };
@@ -90,28 +88,6 @@ constexpr uint32_t f16_idesc() {
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-// Thread-block cluster: barrier over all threads of all CTAs, rank, and
-// loads from another CTA's shared memory.
-__device__ __forceinline__ void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t map_cluster(uint32_t local_smem_addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local_smem_addr), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ float2 ld_cluster_f2(uint32_t cluster_addr) {
-    float2 v;
-    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(cluster_addr) : "memory");
-    return v;
-}
-
 template <int BP>
 __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_constant__ CUtensorMap wmap,
                                                               const __grid_constant__ CUtensorMap xmap,
@@ -157,37 +133,6 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
     const uint32_t tmem = tmem_base;
     grid_dependency_wait();
     grid_dependents_launch();
-
-    // ---- this CTA's share of the tile's (token, row pair) items, and the
-    // position, (cos, sin) and block id each needs, loaded now so that the
-    // loads overlap the main loop ------------------------------------------------
-    constexpr int EI = 8;  // items per thread whose inputs are held in registers
-    const int pairs = kQRows / 2;
-    const int HD = a.H * a.D, KD = a.Hkv * a.D;
-    const int items = a.B * pairs;
-    const int rank = (int)cluster_rank();
-    const int i0 = (int)((long long)items * rank / a.splits), i1 = (int)((long long)items * (rank + 1) / a.splits);
-    int mpos[EI], mblk[EI];
-    float2 mcs[EI];
-    auto load_meta = [&](int base) {
-#pragma unroll
-        for (int k = 0; k < EI; ++k) {
-            const int idx = base + k * kQThreads;
-            mpos[k] = -1;
-            mblk[k] = -1;
-            mcs[k] = make_float2(0.f, 0.f);
-            if (idx >= i1) continue;
-            const int t = idx / pairs, n = row0 + 2 * (idx % pairs);
-            const int p = a.pos[t];
-            if (p < 0 || p >= a.max_pos || p >= a.maxb * a.bs) continue;
-            mpos[k] = p;
-            if (n < HD + KD)
-                mcs[k] = *reinterpret_cast<const float2*>(a.cos_sin + ((size_t)p * (a.D / 2) + (n % a.D) / 2) * 2);
-            if (n >= HD) mblk[k] = a.bt[(size_t)t * a.maxb + p / a.bs];
-        }
-    };
-    const bool has_role = threadIdx.x == 0 || threadIdx.x == 32;  // the producer and the MMA issuer start at once
-    if (!has_role) load_meta(i0 + (int)threadIdx.x);
 
     if (threadIdx.x == 0) {
         // ---- producer: weights and activations of stage i ----------------
@@ -247,24 +192,22 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
         else
             mbar_arrive(done);
     }
-    if (has_role) load_meta(i0 + (int)threadIdx.x);
     __syncwarp();
     const bool got = mbar_wait_bounded(done, 0);
     tc_fence_after();
     const bool ok = __syncthreads_and(got) && !failed;
     if (!ok && threadIdx.x == 0) {
-        // the other CTAs of the cluster still count on this one: report, let the
-        // copies still in flight land (bounded), and go on with zero partials
+        // report, let the copies still in flight land (bounded), and go on
+        // with zero partials
         report(a.status, COTTUS_STATUS_TIMEOUT);
         for (int i = consumed; i < issued; ++i) (void)mbar_wait_bounded(&full[i % kQStages], (i / kQStages) & 1);
     }
     __syncthreads();
 
-    // ---- this split's partials into shared memory: red[token][row] ----------
-    // (the stage buffers are free: every multiply has completed)
-    float* red = reinterpret_cast<float*>(smem);
+    // ---- this split's partials: TMEM lane = weight row, column = token -------
     {
-        const int r = warp * 32 + lane;
+        const int r = row0 + warp * 32 + lane;
+        float* p = a.part + (size_t)split * a.B * a.N;
 #pragma unroll
         for (int c0 = 0; c0 < BP; c0 += 16) {
             uint32_t v[16];
@@ -282,80 +225,72 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
                 for (int j = 0; j < 16; ++j) v[j] = 0u;  // an empty (or failed) split contributes zeros
             }
 #pragma unroll
-            for (int j = 0; j < 16; ++j) red[(c0 + j) * kQRows + r] = __uint_as_float(v[j]);
+            for (int j = 0; j < 16; ++j)
+                if (c0 + j < a.B) p[(size_t)(c0 + j) * a.N + r] = __uint_as_float(v[j]);
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
-    cluster_sync();  // every split's partials are in place
+}
 
-    // ---- finish this CTA's items: sum the splits, rotate, store ----------------
-    const uint32_t red_local = smem_addr(red);
-    for (int base = i0 + (int)threadIdx.x, chunk = 0; base < i1; base += EI * kQThreads, ++chunk) {
-        if (chunk > 0) load_meta(base);
-        // the EI items' partial sums from every split, one split at a time with
-        // the EI loads in flight together, added in split order
-        float2 sum[EI];
+// One thread per (token, row pair): the splits added in order, then RoPE,
+// the rotated query and the append.
+__global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvArgs a) {
+    grid_dependency_wait();  // the partials of the projection kernel are complete
+    grid_dependents_launch();
+    const int pairs_all = a.N / 2;
+    const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (idx >= (long long)a.B * pairs_all) return;
+    const int t = (int)(idx / pairs_all), n = 2 * (int)(idx % pairs_all);
+    const int HD = a.H * a.D, KD = a.Hkv * a.D;
+    const int p = a.pos[t];
+    float2 pv[8];
 #pragma unroll
-        for (int k = 0; k < EI; ++k) sum[k] = make_float2(0.f, 0.f);
-        for (int s2 = 0; s2 < a.splits; ++s2) {
-            float2 pv[EI];
+    for (int s = 0; s < 8; ++s)
+        pv[s] = s < a.splits ? __ldcg(reinterpret_cast<const float2*>(a.part + ((size_t)s * a.B + t) * a.N + n))
+                             : make_float2(0.f, 0.f);
+    float v0 = 0.f, v1 = 0.f;
 #pragma unroll
-            for (int k = 0; k < EI; ++k) {
-                const int idx = base + k * kQThreads;
-                const int t = idx / pairs, n = row0 + 2 * (idx % pairs);
-                pv[k] = idx < i1 ? ld_cluster_f2(map_cluster(red_local + (uint32_t)((t * kQRows + (n - row0)) * 4),
-                                                             (uint32_t)s2))
-                                 : make_float2(0.f, 0.f);
-            }
-#pragma unroll
-            for (int k = 0; k < EI; ++k) {
-                sum[k].x = __fadd_rn(sum[k].x, pv[k].x);
-                sum[k].y = __fadd_rn(sum[k].y, pv[k].y);
-            }
+    for (int s = 0; s < 8; ++s)
+        if (s < a.splits) {  // splits added in order
+            v0 = __fadd_rn(v0, pv[s].x);
+            v1 = __fadd_rn(v1, pv[s].y);
         }
-#pragma unroll
-        for (int k = 0; k < EI; ++k) {
-            const int idx = base + k * kQThreads;
-            if (idx >= i1) break;
-            const int t = idx / pairs, n = row0 + 2 * (idx % pairs);
-            float v0 = sum[k].x, v1 = sum[k].y;
-            if (a.qkv_out) *reinterpret_cast<float2*>(a.qkv_out + (size_t)t * a.N + n) = make_float2(v0, v1);
-            const int p = mpos[k];
-            if (p < 0) {
-                if ((idx % pairs) == 0) report(a.status, COTTUS_STATUS_BAD_POSITION);
-                continue;
-            }
-            const int d = n % a.D;
-            if (n < HD + KD) rope_pair(v0, v1, mcs[k].x, mcs[k].y, v0, v1);  // q or k: the pair (d, d + 1)
-            if (n < HD) {
-                const size_t e = (size_t)t * HD + n;
-                if (a.q_out_f16) {
-                    reinterpret_cast<__half*>(a.q_out)[e] = __float2half_rn(v0);
-                    reinterpret_cast<__half*>(a.q_out)[e + 1] = __float2half_rn(v1);
-                } else {
-                    reinterpret_cast<float*>(a.q_out)[e] = v0;
-                    reinterpret_cast<float*>(a.q_out)[e + 1] = v1;
-                }
-                continue;
-            }
-            const bool is_v = n >= HD + KD;
-            const int kvh = (n - HD - (is_v ? KD : 0)) / a.D;
-            const int blk = mblk[k];
-            if (blk < 0 || (long long)blk >= a.num_blocks) {
-                if ((idx % pairs) == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
-                continue;
-            }
-            // [block][layer][K|V][slot][kv head][dim] (generic_transformer.cpp:234-281)
-            const size_t o = ((((size_t)blk * a.L + a.layer) * 2 + (is_v ? 1 : 0)) * a.bs + (p % a.bs)) * KD +
-                             (size_t)kvh * a.D + d;
-            a.kv[o] = f32_to_f16_trunc(v0);
-            a.kv[o + 1] = f32_to_f16_trunc(v1);
-        }
+    if (a.qkv_out) *reinterpret_cast<float2*>(a.qkv_out + (size_t)t * a.N + n) = make_float2(v0, v1);
+    if (p < 0 || p >= a.max_pos || p >= a.maxb * a.bs) {
+        if (n == 0) report(a.status, COTTUS_STATUS_BAD_POSITION);
+        return;
     }
-    cluster_sync();  // no CTA leaves while others may still read its partials
+    const int d = n % a.D;
+    if (n < HD + KD) {  // q or k: rotate the interleaved pair (d, d + 1)
+        const float2 cs = *reinterpret_cast<const float2*>(a.cos_sin + ((size_t)p * (a.D / 2) + d / 2) * 2);
+        rope_pair(v0, v1, cs.x, cs.y, v0, v1);
+    }
+    if (n < HD) {
+        const size_t e = (size_t)t * HD + n;
+        if (a.q_out_f16) {
+            reinterpret_cast<__half*>(a.q_out)[e] = __float2half_rn(v0);
+            reinterpret_cast<__half*>(a.q_out)[e + 1] = __float2half_rn(v1);
+        } else {
+            reinterpret_cast<float*>(a.q_out)[e] = v0;
+            reinterpret_cast<float*>(a.q_out)[e + 1] = v1;
+        }
+        return;
+    }
+    const bool is_v = n >= HD + KD;
+    const int kvh = (n - HD - (is_v ? KD : 0)) / a.D;
+    const int blk = a.bt[(size_t)t * a.maxb + p / a.bs];
+    if (blk < 0 || (long long)blk >= a.num_blocks) {
+        if (n == HD) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
+        return;
+    }
+    // [block][layer][K|V][slot][kv head][dim] (generic_transformer.cpp:234-281)
+    const size_t o = ((((size_t)blk * a.L + a.layer) * 2 + (is_v ? 1 : 0)) * a.bs + (p % a.bs)) * KD +
+                     (size_t)kvh * a.D + d;
+    a.kv[o] = f32_to_f16_trunc(v0);
+    a.kv[o + 1] = f32_to_f16_trunc(v1);
 }
 
 template <int BP>
@@ -375,55 +310,44 @@ cudaError_t launch_qkv(const CUtensorMap& wmap, const CUtensorMap& xmap, const Q
     cfg.blockDim = dim3(kQThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;  // the splits of a row tile
-    attr[1].val.clusterDim.x = 1;
-    attr[1].val.clusterDim.y = a.splits;
-    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    return cudaLaunchKernelEx(&cfg, kern, wmap, xmap, a);
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, wmap, xmap, a);
+    if (e != cudaSuccess) return e;
+    const long long items = (long long)a.B * (a.N / 2);
+    cudaLaunchConfig_t fc = cfg;
+    fc.gridDim = dim3((unsigned)((items + 255) / 256));
+    fc.blockDim = dim3(256);
+    fc.dynamicSmemBytes = 0;
+    return cudaLaunchKernelEx(&fc, qkv_finish_kernel, a);
 }
 
-// Splits of K: one cluster of `splits` CTAs per row tile (at most 8, the
-// portable cluster size), as many as still let every cluster of the grid be
-// resident at once (clusters are placed whole inside a GPC, so that count
-// comes from the occupancy API rather than from SMs x CTAs per SM).
+// Splits of K so that the grid fits in one wave (resident CTAs per SM from
+// the occupancy API), at most 8.
 template <int BP>
 int splits_for(int row_tiles, int ksteps) {
-    static int cache[64][9] = {};  // [device][splits] -> max active clusters (+1)
+    static int cache[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    auto kern = qkv_proj_kernel<BP>;
-    const size_t smem = qkv_smem_bytes<BP>();
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    for (int s = (ksteps < 8 ? ksteps : 8); s > 1; --s) {
-        int active = 0;
-        if (dev >= 0 && dev < 64 && cache[dev][s]) {
-            active = cache[dev][s] - 1;
-        } else {
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(row_tiles, s);
-            cfg.blockDim = dim3(kQThreads);
-            cfg.dynamicSmemBytes = smem;
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = 1;
-            attr[0].val.clusterDim.y = s;
-            attr[0].val.clusterDim.z = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            if (cudaOccupancyMaxActiveClusters(&active, kern, &cfg) != cudaSuccess) {
-                (void)cudaGetLastError();
-                active = 0;
-            }
-            if (dev >= 0 && dev < 64) cache[dev][s] = active + 1;
-        }
-        if (active >= row_tiles) return s;
+    int per_sm = 1;
+    if (dev >= 0 && dev < 64 && cache[dev]) {
+        per_sm = cache[dev];
+    } else {
+        auto kern = qkv_proj_kernel<BP>;
+        const size_t smem = qkv_smem_bytes<BP>();
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kQThreads, smem) != cudaSuccess ||
+            per_sm < 1)
+            per_sm = 1;
+        if (dev >= 0 && dev < 64) cache[dev] = per_sm;
     }
-    return 1;
+    int s = device_sm_count(dev) * per_sm / row_tiles;
+    if (s > 8) s = 8;
+    if (s > ksteps) s = ksteps;
+    return s < 1 ? 1 : s;
 }
 
 int fail(int code, const std::string& msg) { return set_error(code, msg); }
@@ -435,8 +359,16 @@ int fail(int code, const std::string& msg) { return set_error(code, msg); }
 extern "C" {
 
 size_t cottus_qkv_rope_append_workspace_size(const cottus_qkv_params* p) {
-    (void)p;
-    return 0;  // split partials stay in the shared memory of each row tile's cluster
+    using namespace cb200;
+    if (!p || p->batch <= 0 || p->hidden <= 0 || p->head_dim <= 0) return 0;
+    const long long N = (long long)(p->num_heads + 2 * p->num_kv_heads) * p->head_dim;
+    const int row_tiles = (int)(N / kQRows), ksteps = p->hidden / kQK;
+    if (row_tiles <= 0 || ksteps <= 0) return 0;
+    const int B = p->batch < kQMaxTokens ? p->batch : kQMaxTokens;
+    const int BP = B <= 16 ? 16 : (B <= 32 ? 32 : 64);
+    const int S = BP == 16 ? splits_for<16>(row_tiles, ksteps)
+                           : (BP == 32 ? splits_for<32>(row_tiles, ksteps) : splits_for<64>(row_tiles, ksteps));
+    return (size_t)S * B * N * sizeof(float);  // split partials of one launch of at most 64 tokens
 }
 
 int cottus_qkv_rope_append(const cottus_qkv_params* p, cottus_stream_t stream) {
@@ -458,6 +390,10 @@ int cottus_qkv_rope_append(const cottus_qkv_params* p, cottus_stream_t stream) {
         return fail(COTTUS_ERR_INVALID_ARGUMENT, "x and weight must be 16-byte aligned");
     if (p->query_out_dtype != COTTUS_F16 && p->query_out_dtype != COTTUS_F32)
         return fail(COTTUS_ERR_INVALID_ARGUMENT, "unknown dtype");
+    const size_t need = cottus_qkv_rope_append_workspace_size(p);
+    if (!p->workspace || p->workspace_bytes < need || (reinterpret_cast<uintptr_t>(p->workspace) & 15))
+        return fail(COTTUS_ERR_WORKSPACE, "workspace missing, unaligned or smaller than the required " +
+                                              std::to_string(need) + " bytes");
     const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int row_tiles = (int)(N / kQRows), ksteps = p->hidden / kQK;
     cudaError_t err = cudaSuccess;
@@ -494,6 +430,7 @@ int cottus_qkv_rope_append(const cottus_qkv_params* p, cottus_stream_t stream) {
         a.qkv_out = p->qkv_out ? p->qkv_out + (size_t)b0 * N : nullptr;
         const int S = BP == 16 ? splits_for<16>(row_tiles, ksteps)
                                : (BP == 32 ? splits_for<32>(row_tiles, ksteps) : splits_for<64>(row_tiles, ksteps));
+        a.part = static_cast<float*>(p->workspace);
         a.splits = S;
         a.ksteps = ksteps;
         a.ks_per_split = (ksteps + S - 1) / S;

@@ -241,7 +241,7 @@ typedef struct {
     void *query_out;            /* [batch][num_heads][head_dim] rotated query */
     int32_t query_out_dtype;    /* enum cottus_dtype */
     float *qkv_out;             /* optional [batch][rows] fp32 projections before rotation */
-    void *workspace;            /* unused: cottus_qkv_rope_append_workspace_size() is 0 */
+    void *workspace;            /* cottus_qkv_rope_append_workspace_size() bytes, 16-B aligned, any contents */
     size_t workspace_bytes;
     uint32_t *status;           /* optional device word */
 } cottus_qkv_params;
