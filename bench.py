@@ -174,20 +174,22 @@ def run_reference(args, rank, world):
     import torch
     if world > 1 and rank != 0:
         return
-    if args.config == "qkv_llama3_8b":
+    if args.config in ("qkv_llama3_8b", "oproj_llama3_8b"):
+        qkv = args.config == "qkv_llama3_8b"
         budget = min(2.0, 60.0 / max(args.steps + args.warmup, 1))
         rates, sample, threads = [], "", 1
         t0 = time.perf_counter()
         for i in range(args.warmup + args.steps):
-            r, threads, sample = qkv_reference_rate(target_s=budget)
+            r, threads, sample = (qkv_reference_rate if qkv else oproj_reference_rate)(target_s=budget)
             if i >= args.warmup:
                 rates.append(r)
         v = float(np.mean(rates))
-        print(json.dumps({"metric": "fused QKV+RoPE+append tokens/s", "value": v, "unit": "tokens/s", "n_gpus": world,
+        metric = "fused QKV+RoPE+append tokens/s" if qkv else "O-projection+residual tokens/s"
+        print(json.dumps({"metric": metric, "value": v, "unit": "tokens/s", "n_gpus": world,
                           "steps": args.steps, "warmup": args.warmup,
                           "ms_per_step": (time.perf_counter() - t0) / max(args.steps + args.warmup, 1) * 1e3,
                           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-                          "data": "synthetic", "config": {"workload": "qkv_llama3_8b"}, "impl": "reference",
+                          "data": "synthetic", "config": {"workload": args.config}, "impl": "reference",
                           "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference",
                                            "sample": sample},
                           "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
@@ -233,6 +235,87 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def timed_steps(step, args, dev, world, local):
+    """W untimed steps, then K steps between CUDA events on the current
+    stream with the SM clocks sampled; max over ranks.  Returns (ms per step, clocks)."""
+    import torch
+    import torch.distributed as dist
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    return max_over_ranks(e0.elapsed_time(e1) / args.steps, dev, world), clocks
+
+
+def graph_of_steps(step, n, dev):
+    """A CUDA graph of steps 0..n-1 (one per layer's weights): the projection
+    kernels take a few microseconds, less than a host-side call through the
+    ctypes layer, so the device-timed loop replays the launches as a graph,
+    as a decode engine does.  Steps run once outside the capture first (the
+    cached workspace and the kernel attributes are set up there)."""
+    import torch
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for i in range(n):
+            step(i)
+    torch.cuda.current_stream(dev).wait_stream(side)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(n):
+            step(i)
+    torch.cuda.synchronize(dev)
+    return g
+
+
+def e2e_steps(step, x, y, args, dev, world):
+    """Each step: x's values from pinned host memory, step(i, device copy), y
+    read back into pinned host memory; ms per step between CUDA events, max over ranks."""
+    import torch
+    stream = torch.cuda.current_stream(dev)
+    hx = x.cpu().pin_memory()
+    hy = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+    dx = torch.empty_like(x)
+    n_e2e = max(min(args.steps // 5, 2000), 10)
+    for i in range(3):
+        dx.copy_(hx, non_blocking=True)
+        step(i, dx)
+        hy.copy_(y, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for i in range(n_e2e):
+        dx.copy_(hx, non_blocking=True)
+        step(i, dx)
+        hy.copy_(y, non_blocking=True)
+    b.record(stream)
+    torch.cuda.synchronize(dev)
+    return max_over_ranks(a.elapsed_time(b) / n_e2e, dev, world)
+
+
+def max_over_ranks(v, dev, world):
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
 QKV = dict(hidden=4096, H=32, Hkv=8, D=128, B=64, layers=4, bs=16, maxb=128)  # Llama-3-8B projection, batch 64
 
 
@@ -270,56 +353,20 @@ def run_qkv(args, rank, world, local):
     tab = cb.rope_cos_sin_table(q["maxb"] * q["bs"], q["D"]).to(dev)
     pool = torch.zeros(nb * 2 * q["layers"] * q["bs"] * q["Hkv"] * q["D"], dtype=torch.int16, device=dev)
     qout = torch.empty((q["B"], q["H"], q["D"]), dtype=torch.float16, device=dev)
-    stream = torch.cuda.current_stream(dev)
     kw = dict(num_heads=q["H"], num_kv_heads=q["Hkv"], head_dim=q["D"], block_size=q["bs"], num_layers=q["layers"],
               num_physical_blocks=nb, query_out=qout)
 
     def step(i, xx=x):
         cb.qkv_rope_append(xx, ws[i % q["layers"]], pos, tab, pool, table, layer=i % q["layers"], **kw)
 
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for i in range(args.steps):
-        step(i)
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    clocks = sampler.stop()
-    ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        tt = torch.tensor([ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        ms = float(tt.item())
+    g = graph_of_steps(step, q["layers"], dev)
+    reps = max(args.steps // q["layers"], 1)
+    args_g = argparse.Namespace(**{**vars(args), "steps": reps, "warmup": max(args.warmup // q["layers"], 3)})
+    ms, clocks = timed_steps(lambda i: g.replay(), args_g, dev, world, local)
+    ms /= q["layers"]
+    steps_timed = reps * q["layers"]
     # end to end: the step's activations from pinned host memory, the rotated query back
-    hx = x.cpu().pin_memory()
-    hq = torch.empty(qout.shape, dtype=qout.dtype).pin_memory()
-    dx = torch.empty_like(x)
-    n_e2e = max(min(args.steps // 5, 2000), 10)
-    for i in range(3):
-        dx.copy_(hx, non_blocking=True)
-        step(i, dx)
-        hq.copy_(qout, non_blocking=True)
-    torch.cuda.synchronize(dev)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for i in range(n_e2e):
-        dx.copy_(hx, non_blocking=True)
-        step(i, dx)
-        hq.copy_(qout, non_blocking=True)
-    b.record(stream)
-    torch.cuda.synchronize(dev)
-    e_ms = a.elapsed_time(b) / n_e2e
-    if world > 1:
-        tt = torch.tensor([e_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        e_ms = float(tt.item())
+    e_ms = e2e_steps(step, x, qout, args, dev, world)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r, cores, sample = qkv_reference_rate(target_s=6.0)
@@ -334,7 +381,7 @@ def run_qkv(args, rank, world, local):
     alg = wbytes + x.numel() * 2 + qout.numel() * 2 + q["B"] * 2 * q["Hkv"] * q["D"] * 2 + q["B"] * 8
     line = {
         "metric": "fused QKV+RoPE+append tokens/s", "value": world * q["B"] / (ms * 1e-3), "unit": "tokens/s",
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "n_gpus": world, "steps": steps_timed, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16 x f16 -> f32",
         "data": "synthetic: seeded N(0,1) activations, N(0, 1/hidden) fp16 weights",
         "config": {"workload": f"qkv_llama3_8b: hidden {q['hidden']} -> {N} rows (H{q['H']}/Hkv{q['Hkv']}/D{q['D']}), "
@@ -343,14 +390,16 @@ def run_qkv(args, rank, world, local):
                    "parallelism": f"replicas on {world} GPU(s), no collective"},
         "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": alg / (ms * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
-                     "kernel": "qkv_proj_kernel: one launch per step", "kernel_ms": ms, "algorithmic_bytes": alg},
+                     "kernel": "qkv_proj_kernel + qkv_finish_kernel per step (CUDA graph of 4 layers' steps)",
+                     "kernel_ms": ms, "algorithmic_bytes": alg},
         "cpu_baseline": cpu,
         "e2e": {"value": world * q["B"] / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": qout.numel() * 2, "ms_per_step": e_ms,
                 "api": "cottus_qkv_rope_append (C ABI via ctypes)"},
-        "gpu_launches": args.steps, "clocks": clocks,
+        "gpu_launches": 2 * steps_timed, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
+    del g
     if world > 1:
         dist.destroy_process_group()
 
@@ -387,6 +436,108 @@ def qkv_reference_rate(target_s=6.0, tokens=None):
     return done / el, threads, f"{done} tokens x 1 layer ({el:.1f} s wall, {threads} threads)"
 
 
+OPROJ = dict(fin=4096, fout=4096, B=64, layers=8)  # Llama-3-8B output projection, batch 64
+
+
+def run_oproj(args, rank, world, local):
+    """Output projection + residual add (cottus_o_proj_residual) on the
+    Llama-3-8B shape (4096 -> 4096), batch 64, in place on the fp32 residual
+    stream; each step one layer, cycling over 8 layers' weights (268 MB > L2).
+    Replicas per GPU (weak scaling, no collective)."""
+    import torch
+    import torch.distributed as dist
+    import cottus_b200 as cb
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    o = OPROJ
+    g = torch.Generator(device="cpu").manual_seed(11)
+    x = torch.randn((o["B"], o["fin"]), generator=g).half().to(dev)
+    ws = [(torch.randn((o["fout"], o["fin"]), generator=g) / o["fin"] ** 0.5).half().to(dev)
+          for _ in range(o["layers"])]
+    resid = torch.randn((o["B"], o["fout"]), generator=g).to(dev)
+
+    def step(i, xx=x):
+        cb.o_proj_residual(xx, ws[i % o["layers"]], resid, out=resid)
+
+    g = graph_of_steps(step, o["layers"], dev)
+    reps = max(args.steps // o["layers"], 1)
+    args_g = argparse.Namespace(**{**vars(args), "steps": reps, "warmup": max(args.warmup // o["layers"], 3)})
+    ms, clocks = timed_steps(lambda i: g.replay(), args_g, dev, world, local)
+    ms /= o["layers"]
+    steps_timed = reps * o["layers"]
+    # end to end: the attention output from pinned host memory, the residual stream back
+    e_ms = e2e_steps(step, x, resid, args, dev, world)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r, cores, sample = oproj_reference_rate(target_s=6.0)
+        cpu = {"value": r, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample}
+    if world > 1:
+        dist.barrier()
+        if rank != 0:
+            dist.destroy_process_group()
+            return
+    peak, peak_kind = peaks()
+    wbytes = o["fout"] * o["fin"] * 2
+    alg = wbytes + x.numel() * 2 + 2 * resid.numel() * 4
+    line = {
+        "metric": "O-projection+residual tokens/s", "value": world * o["B"] / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps_timed, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 x f16 -> f32",
+        "data": "synthetic: seeded N(0,1) activations and residual, N(0, 1/in) fp16 weights",
+        "config": {"workload": f"oproj_llama3_8b: {o['fin']} -> {o['fout']}, batch {o['B']}, "
+                               f"one of {o['layers']} layers per step, in place on the fp32 residual",
+                   "l2": f"{o['layers']} layers' weights ({o['layers'] * wbytes / 1e6:.0f} MB) cycled, > 126 MB L2",
+                   "parallelism": f"replicas on {world} GPU(s), no collective"},
+        "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": alg / (ms * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "qkv_proj_kernel (GEMM) + oproj_finish_kernel per step (CUDA graph of 8 layers' steps)",
+                     "kernel_ms": ms,
+                     "algorithmic_bytes": alg},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * o["B"] / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 2,
+                "d2h_bytes_per_step": resid.numel() * 4, "ms_per_step": e_ms,
+                "api": "cottus_o_proj_residual (C ABI via ctypes)"},
+        "gpu_launches": 2 * steps_timed, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    del g
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def oproj_reference_rate(target_s=6.0):
+    """The reference's CPU step for one token and one layer: gemmCPU with wo
+    (fp32, [in][out]) then residualAddCPU (generic_transformer.cpp:305-327),
+    tokens spread over the host threads; returns (tokens/s, threads, sample)."""
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle.oracle import Reference
+
+    o = OPROJ
+    ref = Reference()
+    rng = np.random.default_rng(4)
+    wt = rng.standard_normal((o["fin"], o["fout"]), dtype=np.float32) / np.float32(o["fin"] ** 0.5)
+    threads = os.cpu_count() or 1
+    xs = rng.standard_normal((threads, o["fin"]), dtype=np.float32)
+    res = rng.standard_normal((threads, o["fout"]), dtype=np.float32)
+
+    def one(i):
+        res[i] += ref.gemm(xs[i:i + 1], wt)[0]
+
+    done, t0 = 0, time.perf_counter()
+    with ThreadPoolExecutor(threads) as ex:
+        while True:
+            list(ex.map(one, range(threads)))
+            done += threads
+            el = time.perf_counter() - t0
+            if el >= target_s:
+                break
+    return done / el, threads, f"{done} tokens x 1 layer ({el:.1f} s wall, {threads} threads)"
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -395,7 +546,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="llama3_8b",
                     choices=["tinyllama_f32", "llama3_8b", "ragged_mha", "long_ctx_70b", "fused_tinyllama",
-                             "qkv_llama3_8b"])
+                             "qkv_llama3_8b", "oproj_llama3_8b"])
     ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -416,6 +567,9 @@ def main():
         return
     if args.config == "qkv_llama3_8b":
         run_qkv(args, rank, world, local)
+        return
+    if args.config == "oproj_llama3_8b":
+        run_oproj(args, rank, world, local)
         return
 
     import cottus_b200 as cb

@@ -79,6 +79,14 @@ class QkvParams(C.Structure):
     ]
 
 
+class OProjParams(C.Structure):
+    _fields_ = [
+        ("x", _vp), ("weight", _vp), ("in_features", _i32), ("out_features", _i32), ("batch", _i32),
+        ("residual", _vp), ("out", _vp), ("out_dtype", _i32),
+        ("workspace", _vp), ("workspace_bytes", _sz), ("status", _vp),
+    ]
+
+
 class CottusError(RuntimeError):
     def __init__(self, code: int, message: str):
         super().__init__(f"{message} (code {code})")
@@ -121,6 +129,8 @@ def lib() -> C.CDLL:
         ("cottus_block_allocator_total_blocks", _i32, [_vp]),
         ("cottus_qkv_rope_append_workspace_size", _sz, [P(QkvParams)]),
         ("cottus_qkv_rope_append", C.c_int, [P(QkvParams), _vp]),
+        ("cottus_o_proj_residual_workspace_size", _sz, [P(OProjParams)]),
+        ("cottus_o_proj_residual", C.c_int, [P(OProjParams), _vp]),
         ("cottus_peer_exchange_create", C.c_int, [_i32, _i32, _i32, _i32, _i32, P(_vp), _vp]),
         ("cottus_peer_exchange_open", C.c_int, [_vp, _vp]),
         ("cottus_peer_exchange_destroy", None, [_vp]),

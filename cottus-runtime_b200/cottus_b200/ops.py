@@ -12,7 +12,7 @@ import torch
 
 from . import _lib
 from ._lib import (F16, F32, CottusError, DecodeBatchDesc, DecodeStepParams, LseCombineParams, PagedDecodeParams,
-                   QkvParams, check, lib)
+                   OProjParams, QkvParams, check, lib)
 
 _DT = {torch.float32: F32, torch.float16: F16}
 
@@ -227,6 +227,28 @@ def qkv_rope_append(x, weight, positions, cos_sin, kv_pool, block_table, *, num_
         p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
     check(lib().cottus_qkv_rope_append(C.byref(p), _stream(stream)))
     return query_out
+
+
+def o_proj_residual(x, weight, residual, *, out=None, out_dtype=torch.float32, status=None, stream=None):
+    """Output projection + residual add (cottus_o_proj_residual):
+    out = x . weight^T + residual.  x [B][in] fp16, weight [out][in] fp16,
+    residual [B][out] fp32; out may be the residual tensor itself (fp32)."""
+    for t, n in ((x, "x"), (weight, "weight"), (residual, "residual")):
+        _require(t, n)
+    B, fin = x.shape
+    fout = weight.shape[0]
+    if out is None:
+        out = torch.empty((B, fout), dtype=out_dtype, device=x.device)
+    p = OProjParams()
+    p.x, p.weight, p.in_features, p.out_features, p.batch = x.data_ptr(), weight.data_ptr(), fin, fout, B
+    p.residual, p.out, p.out_dtype = residual.data_ptr(), out.data_ptr(), _dtype_code(out)
+    p.status = status.data_ptr() if status is not None else None
+    need = lib().cottus_o_proj_residual_workspace_size(C.byref(p))
+    if need:
+        ws = workspace(need, x.device)
+        p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
+    check(lib().cottus_o_proj_residual(C.byref(p), _stream(stream)))
+    return out
 
 
 def paged_gather(kv_pool, block_table, context_lens, *, max_context, num_kv_heads, head_dim, block_size,

@@ -1,5 +1,7 @@
-// The step before the attention path, fused: QKV projection of each
-// sequence's new token, RoPE on q and k, and the KV-cache append.
+// The steps either side of the attention path on the tensor cores: the QKV
+// projection of each sequence's new token fused with RoPE on q and k and
+// the KV-cache append (before), and the output projection fused with the
+// residual add (after, generic_transformer.cpp:305-325).
 //
 // Replaces, per layer and token, generic_transformer.cpp:169-284: three
 // gemmCUDA calls (cuBLAS SGEMM, compute_primitives_cuda.cu:30-55), two
@@ -9,9 +11,9 @@
 // out[t][n] = sum_k x[t][k] * W[n][k] for the batch's tokens t (at most 64
 // per launch, more are chunked by the host) and the stacked rows n of Wq,
 // Wk, Wv.  The op streams the weights once, so HBM bandwidth bounds it:
-//   * CTA tile: 128 weight rows x all tokens (padded to 16, 32 or 64), a
-//     split of the K range; grid = (rows/128) x splits, splits chosen so the
-//     grid fits in one wave of two CTAs per SM;
+//   * CTA tile: 128 weight rows x all tokens (padded to 16, 32 or 64), every
+//     splits-th 64-wide k-step; grid = (rows/128) x splits, splits (at most
+//     16) chosen so the grid fills one wave of two CTAs per SM;
 //   * weights and activations staged by TMA in 64-element (128-byte) rows
 //     with 128B swizzle through a 4-stage mbarrier ring (warp 0 produces;
 //     two CTAs per SM);
@@ -49,6 +51,7 @@ constexpr int kQK = 64;      // k elements per stage (one 128-byte swizzled row)
 constexpr int kQStages = 4;  // ring depth (two CTAs per SM)
 constexpr int kQThreads = 128;
 constexpr int kQMaxTokens = 64;
+constexpr int kQMaxSplits = 16;
 
 struct QkvArgs {
     const uint16_t* w;
@@ -62,8 +65,11 @@ struct QkvArgs {
     int q_out_f16;
     float* qkv_out;
     float* part;  // [splits][B][N]
-    int splits, ksteps, ks_per_split;
+    int splits, ksteps;
     uint32_t* status;
+    const float* residual;  // O-projection: [B][N] added to the product
+    void* out;              // O-projection: [B][N]
+    int out_f16;
 };
 
 template <int BP>
@@ -105,9 +111,13 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int tile = blockIdx.x, split = blockIdx.y;
     const int row0 = tile * kQRows;
-    const int k0 = split * a.ks_per_split;
-    const int k1 = min(k0 + a.ks_per_split, a.ksteps);
-    const int nsteps = k1 > k0 ? k1 - k0 : 0;
+    // k-steps split, split + splits, ...: at any moment the splits of a row
+    // tile read neighbouring 128-byte pieces of the same weight rows
+    const int nsteps = split < a.ksteps ? (a.ksteps - split + a.splits - 1) / a.splits : 0;
+    const int npre = nsteps < kQStages ? nsteps : kQStages;
+    // the finish kernel may become resident now: it holds no shared memory
+    // and waits for this grid to complete before it reads anything
+    grid_dependents_launch();
 
     if (threadIdx.x == 0) {
         prefetch_tensormap(&wmap);
@@ -120,6 +130,12 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
         fence_barrier_init();
         failed = 0;
         issued = consumed = 0;
+        // the weights do not depend on the preceding kernel: the first stages'
+        // tiles are requested before waiting for it
+        for (int i = 0; i < npre; ++i) {
+            mbar_arrive_expect_tx(&full[i], STAGE);
+            tma_load_2d(smem + (size_t)i * STAGE, &wmap, &full[i], (split + i * a.splits) * kQK, row0);
+        }
     }
     if (warp == 0) {  // accumulator: TMEM_COLS columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
@@ -131,8 +147,7 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_base;
-    grid_dependency_wait();
-    grid_dependents_launch();
+    grid_dependency_wait();  // the preceding kernel is complete: activations ready, workspace free
 
     if (threadIdx.x == 0) {
         // ---- producer: weights and activations of stage i ----------------
@@ -143,18 +158,12 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
                 break;
             }
             uint8_t* st = smem + (size_t)slot * STAGE;
-            mbar_arrive_expect_tx(&full[slot], STAGE);
-            const int kx = (k0 + i) * kQK;
-            asm volatile(
-                "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-                    smem_addr(st)),
-                "l"(reinterpret_cast<uint64_t>(&wmap)), "r"(kx), "r"(row0), "r"(smem_addr(&full[slot]))
-                : "memory");
-            asm volatile(
-                "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-                    smem_addr(st + W_BYTES)),
-                "l"(reinterpret_cast<uint64_t>(&xmap)), "r"(kx), "r"(0), "r"(smem_addr(&full[slot]))
-                : "memory");
+            const int kx = (split + i * a.splits) * kQK;
+            if (i >= npre) {
+                mbar_arrive_expect_tx(&full[slot], STAGE);
+                tma_load_2d(st, &wmap, &full[slot], kx, row0);
+            }
+            tma_load_2d(st + W_BYTES, &xmap, &full[slot], kx, 0);
             issued = i + 1;
         }
     } else if (threadIdx.x == 32) {
@@ -200,6 +209,8 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
         // report, let the copies still in flight land (bounded), and go on
         // with zero partials
         report(a.status, COTTUS_STATUS_TIMEOUT);
+        // (the producer waits for nothing before it has requested the
+        // activations of the prefetched stages, so issued >= npre)
         for (int i = consumed; i < issued; ++i) (void)mbar_wait_bounded(&full[i % kQStages], (i / kQStages) & 1);
     }
     __syncthreads();
@@ -238,22 +249,24 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
 // One thread per (token, row pair): the splits added in order, then RoPE,
 // the rotated query and the append.
 __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvArgs a) {
-    grid_dependency_wait();  // the partials of the projection kernel are complete
+    // the next projection may start streaming its weights while this runs;
+    // it waits for this grid before it touches the activations or partials
     grid_dependents_launch();
+    grid_dependency_wait();  // the partials of the projection kernel are complete
     const int pairs_all = a.N / 2;
     const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (idx >= (long long)a.B * pairs_all) return;
     const int t = (int)(idx / pairs_all), n = 2 * (int)(idx % pairs_all);
     const int HD = a.H * a.D, KD = a.Hkv * a.D;
     const int p = a.pos[t];
-    float2 pv[8];
+    float2 pv[kQMaxSplits];
 #pragma unroll
-    for (int s = 0; s < 8; ++s)
+    for (int s = 0; s < kQMaxSplits; ++s)
         pv[s] = s < a.splits ? __ldcg(reinterpret_cast<const float2*>(a.part + ((size_t)s * a.B + t) * a.N + n))
                              : make_float2(0.f, 0.f);
     float v0 = 0.f, v1 = 0.f;
 #pragma unroll
-    for (int s = 0; s < 8; ++s)
+    for (int s = 0; s < kQMaxSplits; ++s)
         if (s < a.splits) {  // splits added in order
             v0 = __fadd_rn(v0, pv[s].x);
             v1 = __fadd_rn(v1, pv[s].y);
@@ -293,18 +306,45 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvArgs a) {
     a.kv[o + 1] = f32_to_f16_trunc(v1);
 }
 
-template <int BP>
-cudaError_t launch_qkv(const CUtensorMap& wmap, const CUtensorMap& xmap, const QkvArgs& a, int row_tiles,
-                       cudaStream_t st) {
+// One thread per (token, column pair) of the O-projection: the splits added
+// in order, then the residual (generic_transformer.cpp:305-325: x = att . Wo,
+// then x = x + xb).
+__global__ void __launch_bounds__(256) oproj_finish_kernel(const QkvArgs a) {
+    grid_dependents_launch();
+    grid_dependency_wait();
+    const int pairs_all = a.N / 2;
+    const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+    if (idx >= (long long)a.B * pairs_all) return;
+    const int t = (int)(idx / pairs_all), n = 2 * (int)(idx % pairs_all);
+    float2 pv[kQMaxSplits];
+#pragma unroll
+    for (int s = 0; s < kQMaxSplits; ++s)
+        pv[s] = s < a.splits ? __ldcg(reinterpret_cast<const float2*>(a.part + ((size_t)s * a.B + t) * a.N + n))
+                             : make_float2(0.f, 0.f);
+    const float2 r = *reinterpret_cast<const float2*>(a.residual + (size_t)t * a.N + n);
+    float v0 = 0.f, v1 = 0.f;
+#pragma unroll
+    for (int s = 0; s < kQMaxSplits; ++s)
+        if (s < a.splits) {
+            v0 = __fadd_rn(v0, pv[s].x);
+            v1 = __fadd_rn(v1, pv[s].y);
+        }
+    v0 = __fadd_rn(v0, r.x);
+    v1 = __fadd_rn(v1, r.y);
+    const size_t e = (size_t)t * a.N + n;
+    if (a.out_f16) {
+        reinterpret_cast<__half*>(a.out)[e] = __float2half_rn(v0);
+        reinterpret_cast<__half*>(a.out)[e + 1] = __float2half_rn(v1);
+    } else {
+        *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.out) + e) = make_float2(v0, v1);
+    }
+}
+
+template <int BP, bool QKV>
+cudaError_t launch_proj(const CUtensorMap& wmap, const CUtensorMap& xmap, const QkvArgs& a, int row_tiles,
+                        cudaStream_t st) {
     auto kern = qkv_proj_kernel<BP>;
     const size_t smem = qkv_smem_bytes<BP>();
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr_set[dev] = true;
-    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(row_tiles, a.splits);
     cfg.blockDim = dim3(kQThreads);
@@ -322,32 +362,47 @@ cudaError_t launch_qkv(const CUtensorMap& wmap, const CUtensorMap& xmap, const Q
     fc.gridDim = dim3((unsigned)((items + 255) / 256));
     fc.blockDim = dim3(256);
     fc.dynamicSmemBytes = 0;
-    return cudaLaunchKernelEx(&fc, qkv_finish_kernel, a);
+    if constexpr (QKV) return cudaLaunchKernelEx(&fc, qkv_finish_kernel, a);
+    else return cudaLaunchKernelEx(&fc, oproj_finish_kernel, a);
 }
 
-// Splits of K so that the grid fits in one wave (resident CTAs per SM from
-// the occupancy API), at most 8.
+// Resident CTAs per SM: the SM's shared memory (the kernel asks for the
+// largest carveout) over what one CTA takes, dynamic + static + the block
+// reserve; 128 threads and a few dozen registers never bind first.
+template <int BP>
+int ctas_per_sm(int dev) {
+    static int cache[64] = {};
+    if (dev >= 0 && dev < 64 && cache[dev]) return cache[dev];
+    auto kern = qkv_proj_kernel<BP>;
+    const size_t smem = qkv_smem_bytes<BP>();
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+    cudaFuncAttributes fa = {};
+    int sm_smem = 0, reserve = 0;
+    int n = 1;
+    if (cudaFuncGetAttributes(&fa, kern) == cudaSuccess &&
+        cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) == cudaSuccess &&
+        cudaDeviceGetAttribute(&reserve, cudaDevAttrReservedSharedMemoryPerBlock, dev) == cudaSuccess)
+        n = (int)((size_t)sm_smem / (smem + fa.sharedSizeBytes + (size_t)reserve));
+    if (n < 1) n = 1;
+    if (dev >= 0 && dev < 64) cache[dev] = n;
+    return n;
+}
+
+// Splits of K so that the grid fills one wave, at most kQMaxSplits.
 template <int BP>
 int splits_for(int row_tiles, int ksteps) {
-    static int cache[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    int per_sm = 1;
-    if (dev >= 0 && dev < 64 && cache[dev]) {
-        per_sm = cache[dev];
-    } else {
-        auto kern = qkv_proj_kernel<BP>;
-        const size_t smem = qkv_smem_bytes<BP>();
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kQThreads, smem) != cudaSuccess ||
-            per_sm < 1)
-            per_sm = 1;
-        if (dev >= 0 && dev < 64) cache[dev] = per_sm;
-    }
-    int s = device_sm_count(dev) * per_sm / row_tiles;
-    if (s > 8) s = 8;
+    int s = device_sm_count(dev) * ctas_per_sm<BP>(dev) / row_tiles;
+    if (s > kQMaxSplits) s = kQMaxSplits;
     if (s > ksteps) s = ksteps;
     return s < 1 ? 1 : s;
+}
+
+int splits_for_tokens(int BP, int row_tiles, int ksteps) {
+    return BP == 16 ? splits_for<16>(row_tiles, ksteps)
+                    : (BP == 32 ? splits_for<32>(row_tiles, ksteps) : splits_for<64>(row_tiles, ksteps));
 }
 
 int fail(int code, const std::string& msg) { return set_error(code, msg); }
@@ -366,8 +421,7 @@ size_t cottus_qkv_rope_append_workspace_size(const cottus_qkv_params* p) {
     if (row_tiles <= 0 || ksteps <= 0) return 0;
     const int B = p->batch < kQMaxTokens ? p->batch : kQMaxTokens;
     const int BP = B <= 16 ? 16 : (B <= 32 ? 32 : 64);
-    const int S = BP == 16 ? splits_for<16>(row_tiles, ksteps)
-                           : (BP == 32 ? splits_for<32>(row_tiles, ksteps) : splits_for<64>(row_tiles, ksteps));
+    const int S = splits_for_tokens(BP, row_tiles, ksteps);
     return (size_t)S * B * N * sizeof(float);  // split partials of one launch of at most 64 tokens
 }
 
@@ -428,16 +482,79 @@ int cottus_qkv_rope_append(const cottus_qkv_params* p, cottus_stream_t stream) {
         a.q_out = static_cast<uint8_t*>(p->query_out) + (size_t)b0 * p->num_heads * p->head_dim * qe;
         a.q_out_f16 = p->query_out_dtype == COTTUS_F16;
         a.qkv_out = p->qkv_out ? p->qkv_out + (size_t)b0 * N : nullptr;
-        const int S = BP == 16 ? splits_for<16>(row_tiles, ksteps)
-                               : (BP == 32 ? splits_for<32>(row_tiles, ksteps) : splits_for<64>(row_tiles, ksteps));
+        const int S = splits_for_tokens(BP, row_tiles, ksteps);
         a.part = static_cast<float*>(p->workspace);
         a.splits = S;
         a.ksteps = ksteps;
-        a.ks_per_split = (ksteps + S - 1) / S;
         a.status = p->status;
-        if (BP == 16) err = launch_qkv<16>(wmap, xmap, a, row_tiles, st);
-        else if (BP == 32) err = launch_qkv<32>(wmap, xmap, a, row_tiles, st);
-        else err = launch_qkv<64>(wmap, xmap, a, row_tiles, st);
+        a.residual = nullptr;
+        a.out = nullptr;
+        a.out_f16 = 0;
+        if (BP == 16) err = launch_proj<16, true>(wmap, xmap, a, row_tiles, st);
+        else if (BP == 32) err = launch_proj<32, true>(wmap, xmap, a, row_tiles, st);
+        else err = launch_proj<64, true>(wmap, xmap, a, row_tiles, st);
+        if (err != cudaSuccess) return fail(COTTUS_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
+    }
+    return COTTUS_OK;
+}
+
+size_t cottus_o_proj_residual_workspace_size(const cottus_o_proj_params* p) {
+    using namespace cb200;
+    if (!p || p->batch <= 0 || p->in_features <= 0 || p->out_features <= 0) return 0;
+    const int row_tiles = p->out_features / kQRows, ksteps = p->in_features / kQK;
+    if (row_tiles <= 0 || ksteps <= 0) return 0;
+    const int B = p->batch < kQMaxTokens ? p->batch : kQMaxTokens;
+    const int BP = B <= 16 ? 16 : (B <= 32 ? 32 : 64);
+    const int S = splits_for_tokens(BP, row_tiles, ksteps);
+    return (size_t)S * B * p->out_features * sizeof(float);
+}
+
+int cottus_o_proj_residual(const cottus_o_proj_params* p, cottus_stream_t stream) {
+    using namespace cb200;
+    if (!p) return fail(COTTUS_ERR_INVALID_ARGUMENT, "params must not be NULL");
+    if (p->batch < 0 || p->in_features <= 0 || p->out_features <= 0)
+        return fail(COTTUS_ERR_INVALID_ARGUMENT, "invalid dimensions");
+    if (p->batch == 0) return COTTUS_OK;
+    if (p->in_features % kQK != 0 || p->out_features % kQRows != 0)
+        return fail(COTTUS_ERR_UNSUPPORTED, "in_features must be a multiple of 64 and out_features of 128");
+    if (!p->x || !p->weight || !p->residual || !p->out) return fail(COTTUS_ERR_INVALID_ARGUMENT, "NULL pointer argument");
+    if ((reinterpret_cast<uintptr_t>(p->x) | reinterpret_cast<uintptr_t>(p->weight) |
+         reinterpret_cast<uintptr_t>(p->residual) | reinterpret_cast<uintptr_t>(p->out)) & 15)
+        return fail(COTTUS_ERR_INVALID_ARGUMENT, "x, weight, residual and out must be 16-byte aligned");
+    if (p->out_dtype != COTTUS_F16 && p->out_dtype != COTTUS_F32)
+        return fail(COTTUS_ERR_INVALID_ARGUMENT, "unknown dtype");
+    const size_t need = cottus_o_proj_residual_workspace_size(p);
+    if (!p->workspace || p->workspace_bytes < need || (reinterpret_cast<uintptr_t>(p->workspace) & 15))
+        return fail(COTTUS_ERR_WORKSPACE, "workspace missing, unaligned or smaller than the required " +
+                                              std::to_string(need) + " bytes");
+    const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const int N = p->out_features, K = p->in_features, row_tiles = N / kQRows, ksteps = K / kQK;
+    cudaError_t err = cudaSuccess;
+    const CUtensorMap wmap = make_tensor_map_2d_f16(p->weight, K, N, (uint64_t)K * 2, kQK, kQRows, true, &err);
+    if (err != cudaSuccess) return fail(COTTUS_ERR_CUDA, "weight tensor map rejected");
+    const size_t oe = p->out_dtype == COTTUS_F16 ? 2 : 4;
+    for (int b0 = 0; b0 < p->batch; b0 += kQMaxTokens) {
+        const int B = p->batch - b0 < kQMaxTokens ? p->batch - b0 : kQMaxTokens;
+        const int BP = B <= 16 ? 16 : (B <= 32 ? 32 : 64);
+        const CUtensorMap xmap = make_tensor_map_2d_f16(static_cast<const __half*>(p->x) + (size_t)b0 * K, K, B,
+                                                        (uint64_t)K * 2, kQK, BP, true, &err);
+        if (err != cudaSuccess) return fail(COTTUS_ERR_CUDA, "activation tensor map rejected");
+        QkvArgs a = {};
+        a.w = static_cast<const uint16_t*>(p->weight);
+        a.N = N;
+        a.K = K;
+        a.B = B;
+        a.part = static_cast<float*>(p->workspace);
+        const int S = splits_for_tokens(BP, row_tiles, ksteps);
+        a.splits = S;
+        a.ksteps = ksteps;
+        a.status = p->status;
+        a.residual = p->residual + (size_t)b0 * N;
+        a.out = static_cast<uint8_t*>(p->out) + (size_t)b0 * N * oe;
+        a.out_f16 = p->out_dtype == COTTUS_F16;
+        if (BP == 16) err = launch_proj<16, false>(wmap, xmap, a, row_tiles, st);
+        else if (BP == 32) err = launch_proj<32, false>(wmap, xmap, a, row_tiles, st);
+        else err = launch_proj<64, false>(wmap, xmap, a, row_tiles, st);
         if (err != cudaSuccess) return fail(COTTUS_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
     }
     return COTTUS_OK;

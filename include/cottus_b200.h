@@ -250,6 +250,32 @@ size_t cottus_qkv_rope_append_workspace_size(const cottus_qkv_params *p);
 int cottus_qkv_rope_append(const cottus_qkv_params *p, cottus_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * The step after attention: output projection and residual add, on the
+ * same tensor-core kernel as cottus_qkv_rope_append.  Replaces
+ * generic_transformer.cpp:305-325 per layer and token (gemmCUDA with wo,
+ * then residualAddCUDA):  out[b][n] = (sum_k x[b][k] * weight[n][k]) +
+ * residual[b][n], fp16 x and weight, fp32 accumulation and residual.
+ * in_features a multiple of 64, out_features of 128.  x is typically the
+ * attention output [batch][num_heads*head_dim] (fp16, cottus_paged_decode).
+ * ---------------------------------------------------------------------- */
+typedef struct {
+    const void *x;          /* [batch][in_features] fp16, 16-B aligned */
+    const void *weight;     /* [out_features][in_features] fp16 (the reference's wo [in][out] transposed) */
+    int32_t in_features;
+    int32_t out_features;
+    int32_t batch;
+    const float *residual;  /* [batch][out_features] fp32 (may equal out when out_dtype is fp32) */
+    void *out;              /* [batch][out_features], out_dtype */
+    int32_t out_dtype;      /* enum cottus_dtype */
+    void *workspace;        /* cottus_o_proj_residual_workspace_size() bytes, 16-B aligned, any contents */
+    size_t workspace_bytes;
+    uint32_t *status;       /* optional device word */
+} cottus_o_proj_params;
+
+size_t cottus_o_proj_residual_workspace_size(const cottus_o_proj_params *p);
+int cottus_o_proj_residual(const cottus_o_proj_params *p, cottus_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Block-table gather: copies, bit for bit, the K and V rows of layer
  * `layer` for the first context_lens[b] tokens of each sequence into dense
  * k_out/v_out [batch][max_context][num_kv_heads][head_dim] (fp16 bits);

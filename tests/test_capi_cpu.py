@@ -63,6 +63,28 @@ def test_invalid_arguments_rejected_without_gpu():
     assert L.cottus_status_string(-5) == b"workspace"
 
 
+def test_projection_arguments_rejected_without_gpu():
+    L = _lib.lib()
+    p = _lib.OProjParams()
+    p.in_features, p.out_features, p.batch, p.out_dtype = 128, 256, 3, _lib.F32
+    assert L.cottus_o_proj_residual(None, None) == _lib.COTTUS_ERR_INVALID_ARGUMENT
+    assert L.cottus_o_proj_residual(C.byref(p), None) == _lib.COTTUS_ERR_INVALID_ARGUMENT  # NULL pointers
+    assert "NULL" in L.cottus_last_error().decode()
+    p.x, p.weight, p.residual, p.out = 0x1000, 0x2000, 0x3000, 0x4008
+    assert L.cottus_o_proj_residual(C.byref(p), None) == _lib.COTTUS_ERR_INVALID_ARGUMENT
+    assert "16-byte" in L.cottus_last_error().decode()
+    p.out, p.out_dtype = 0x4000, 9
+    assert L.cottus_o_proj_residual(C.byref(p), None) == _lib.COTTUS_ERR_INVALID_ARGUMENT
+    for fin, fout in [(96, 256), (128, 200)]:
+        q = _lib.OProjParams.from_buffer_copy(p)
+        q.in_features, q.out_features = fin, fout
+        assert L.cottus_o_proj_residual(C.byref(q), None) == _lib.COTTUS_ERR_UNSUPPORTED
+    p.batch = 0
+    assert L.cottus_o_proj_residual(C.byref(p), None) == _lib.COTTUS_OK  # nothing to do
+    p.batch = -1
+    assert L.cottus_o_proj_residual(C.byref(p), None) == _lib.COTTUS_ERR_INVALID_ARGUMENT
+
+
 def test_rope_table_bit_exact(golden):
     r = cases.rope_cases()
     for D, key in ((64, "rope/cos_sin_d64"), (128, "rope/cos_sin_d128")):
