@@ -64,7 +64,7 @@ class DecodeStepParams(C.Structure):
 class DecodeBatchDesc(C.Structure):
     _fields_ = [
         ("num_blocks", _i32), ("block_size", _i32), ("max_batch", _i32), ("max_blocks_per_seq", _i32),
-        ("device_block_table", _vp), ("device_positions", _vp),
+        ("device_block_table", _vp), ("device_positions", _vp), ("device_context_lens", _vp),
     ]
 
 

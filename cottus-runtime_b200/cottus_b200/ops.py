@@ -46,10 +46,13 @@ def _require(t: torch.Tensor, name: str, dtype=None):
 _WS: dict = {}
 
 
-def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+def workspace(nbytes: int, device: torch.device, kind: str = "decode") -> torch.Tensor:
     """Cached scratch buffer (a convenience of this Python layer; the C ABI
-    itself only takes caller-provided workspace)."""
-    key = (device.type, device.index)
+    itself only takes caller-provided workspace).  One buffer per kind: the
+    decode kernels keep the counter words at the start of theirs at zero
+    between calls, while the projections ("proj") overwrite all of theirs
+    with split partials, so the two never share one."""
+    key = (device.type, device.index, kind)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
@@ -223,7 +226,7 @@ def qkv_rope_append(x, weight, positions, cos_sin, kv_pool, block_table, *, num_
     p.status = status.data_ptr() if status is not None else None
     need = lib().cottus_qkv_rope_append_workspace_size(C.byref(p))
     if need:
-        ws = workspace(need, x.device)
+        ws = workspace(need, x.device, "proj")
         p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
     check(lib().cottus_qkv_rope_append(C.byref(p), _stream(stream)))
     return query_out
@@ -245,10 +248,41 @@ def o_proj_residual(x, weight, residual, *, out=None, out_dtype=torch.float32, s
     p.status = status.data_ptr() if status is not None else None
     need = lib().cottus_o_proj_residual_workspace_size(C.byref(p))
     if need:
-        ws = workspace(need, x.device)
+        ws = workspace(need, x.device, "proj")
         p.workspace, p.workspace_bytes = ws.data_ptr(), ws.numel()
     check(lib().cottus_o_proj_residual(C.byref(p), _stream(stream)))
     return out
+
+
+def attention_block(batch, x, w_qkv, w_o, residual, kv_pool, cos_sin, *, num_heads, num_kv_heads, head_dim,
+                    num_layers=1, layer=0, query_out=None, att_out=None, status=None, stream=None):
+    """The attention half of one decoder layer for the step tokens of a
+    DecodeBatch (generic_transformer.cpp:169-327 per token), as three
+    launches of this library: the QKV projection with RoPE and the KV append
+    (cottus_qkv_rope_append), paged decode attention over the device block
+    table with context = position + 1 (cottus_paged_decode), and the output
+    projection added to the residual stream in place (cottus_o_proj_residual).
+
+    x [n][hidden] fp16 (the normalised hidden state of each row's token, n =
+    len(batch)), w_qkv [(H + 2 Hkv) D][hidden] fp16, w_o [hidden][H D] fp16,
+    residual [n][hidden] fp32 (updated in place).  Returns the attention
+    output [n][H D] fp16 (the O-projection's input)."""
+    n = len(batch)
+    if x.shape[0] != n or residual.shape[0] != n:
+        raise ValueError(f"x and residual need one row per active sequence ({n})")
+    nb = batch.num_blocks
+    q = qkv_rope_append(x, w_qkv, batch.positions[:n], cos_sin, kv_pool, batch.block_table[:n], num_heads=num_heads,
+                        num_kv_heads=num_kv_heads, head_dim=head_dim, block_size=batch.block_size,
+                        num_layers=num_layers, layer=layer, num_physical_blocks=nb, query_out=query_out,
+                        query_out_dtype=torch.float16, status=status, stream=stream)
+    if att_out is None:
+        att_out = torch.empty((n, num_heads, head_dim), dtype=torch.float16, device=x.device)
+    paged_decode(q, kv_pool, batch.block_table[:n], batch.context_lens[:n], num_kv_heads=num_kv_heads,
+                 head_dim=head_dim, block_size=batch.block_size, num_layers=num_layers, layer=layer, out=att_out,
+                 status=status, num_physical_blocks=nb, stream=stream)
+    att = att_out.view(n, num_heads * head_dim)
+    o_proj_residual(att, w_o, residual, out=residual, status=status, stream=stream)
+    return att
 
 
 def paged_gather(kv_pool, block_table, context_lens, *, max_context, num_kv_heads, head_dim, block_size,
@@ -305,20 +339,23 @@ class DecodeBatch:
     `device` None keeps the host bookkeeping only.  Per step:
     ``begin_step()``, then per layer ``rope_append_decode(...)`` with
     ``block_table=self.block_table[:n]``, ``positions=self.positions[:n]``
-    (n = len(self)), then ``end_step()``."""
+    (n = len(self)), or ``attention_block(...)``, then ``end_step()``."""
 
     def __init__(self, num_blocks: int, block_size: int, max_batch: int, max_blocks_per_seq: int, device=None):
-        self.block_table = self.positions = None
+        self.block_table = self.positions = self.context_lens = None
         d = DecodeBatchDesc()
         d.num_blocks, d.block_size, d.max_batch, d.max_blocks_per_seq = num_blocks, block_size, max_batch, \
             max_blocks_per_seq
         if device is not None:
             self.block_table = torch.zeros((max_batch, max_blocks_per_seq), dtype=torch.int32, device=device)
             self.positions = torch.zeros(max_batch, dtype=torch.int32, device=device)
+            self.context_lens = torch.zeros(max_batch, dtype=torch.int32, device=device)
             d.device_block_table, d.device_positions = self.block_table.data_ptr(), self.positions.data_ptr()
+            d.device_context_lens = self.context_lens.data_ptr()
         h = C.c_void_p()
         check(lib().cottus_decode_batch_create(C.byref(d), C.byref(h)))
         self._h = h
+        self.num_blocks, self.block_size = num_blocks, block_size
         self.max_batch, self.max_blocks_per_seq = max_batch, max_blocks_per_seq
 
     def add(self, seq_id: int) -> int:

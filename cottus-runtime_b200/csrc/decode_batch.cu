@@ -40,11 +40,15 @@ struct TableUpdates {
 };
 
 __global__ void table_update_kernel(const __grid_constant__ TableUpdates u, int32_t* table, int32_t table_elems,
-                                    int32_t* positions) {
+                                    int32_t* positions, int32_t* context_lens) {
     for (int i = threadIdx.x; i < u.n; i += blockDim.x) {
         const int32_t idx = u.idx[i];
-        if (idx < table_elems) table[idx] = u.val[i];
-        else positions[idx - table_elems] = u.val[i];
+        if (idx < table_elems) {
+            table[idx] = u.val[i];
+        } else {
+            positions[idx - table_elems] = u.val[i];
+            if (context_lens) context_lens[idx - table_elems] = u.val[i] + 1;  // the prefix and the step's token
+        }
     }
 }
 
@@ -100,6 +104,8 @@ int cottus_decode_batch_create(const cottus_decode_batch_desc* desc, cottus_deco
         return fail(COTTUS_ERR_INVALID_ARGUMENT, "block table too large for 32-bit entry indices");
     if (!desc->device_block_table != !desc->device_positions)
         return fail(COTTUS_ERR_INVALID_ARGUMENT, "give both device arrays or neither");
+    if (desc->device_context_lens && !desc->device_positions)
+        return fail(COTTUS_ERR_INVALID_ARGUMENT, "device_context_lens needs the device table and positions");
     try {
         *out = new cottus_decode_batch(*desc);
     } catch (const std::exception& e) {
@@ -203,7 +209,7 @@ int cottus_decode_batch_begin_step(cottus_decode_batch* b, cottus_stream_t strea
                 ++u.n;
             }
             cb200::table_update_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-                u, b->d.device_block_table, b->table_elems(), b->d.device_positions);
+                u, b->d.device_block_table, b->table_elems(), b->d.device_positions, b->d.device_context_lens);
             const cudaError_t e = cudaGetLastError();
             if (e != cudaSuccess) return fail(COTTUS_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(e));
         }

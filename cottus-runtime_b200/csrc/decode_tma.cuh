@@ -373,7 +373,7 @@ __device__ __forceinline__ long long grab_chunk(const TmaArgs& a, long long W, l
 // ps/chunk .. (ps+np-1)/chunk, every one of them non-empty.  Arrives on the
 // pair's counter, tagged with the launch epoch so that a count left by an
 // aborted launch, or bytes of another layout that used the same workspace,
-// read as zero: a compare-and-swap from `hint`, the counter value read a
+// read as zero (a completed pair leaves its counter at zero): a compare-and-swap from `hint`, the counter value read a
 // page earlier, which is right on the first try unless another part arrived
 // in between.  The last arriving worker merges all partials.  Lane items
 // are (head, 8-dim chunk); each lane reads the parts PB at a time with all
@@ -398,9 +398,12 @@ __device__ __forceinline__ void merge_if_last(const TmaArgs& a, int b, int h, lo
         while (true) {  // every failed attempt means another part arrived: at most nparts rounds
             const unsigned long long nv =
                 (unsigned)(old >> 32) == a.epoch ? old + 1 : (((unsigned long long)a.epoch << 32) | 1ull);
-            const unsigned long long prev = atomicCAS(ctr, old, nv);
+            // the last arrival leaves the counter at zero, so that a replay of
+            // this launch (a CUDA graph: same tag) counts from zero again
+            const bool fin = (int)(nv & 0xffffffffull) == nparts;
+            const unsigned long long prev = atomicCAS(ctr, old, fin ? 0ull : nv);
             if (prev == old) {
-                last = (int)(nv & 0xffffffffull) == nparts;
+                last = fin;
                 break;
             }
             old = prev;

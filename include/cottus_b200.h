@@ -319,7 +319,8 @@ int32_t cottus_block_allocator_total_blocks(const cottus_block_allocator *a);
  * needs and sends the changed table entries and the positions to the device
  * (one small kernel on `stream`, parameters passed by value: no device
  * scratch and no copy call); run cottus_rope_append_decode (or
- * cottus_rope_append + cottus_paged_decode) once per layer with
+ * cottus_rope_append / cottus_qkv_rope_append, then cottus_paged_decode with
+ * context_lens = device_context_lens) once per layer with
  * batch = cottus_decode_batch_size(), block_table = device_block_table,
  * positions = device_positions, max_blocks_per_seq as given here; then
  * cottus_decode_batch_end_step advances every position by one.  With both
@@ -338,6 +339,8 @@ typedef struct {
     int32_t max_blocks_per_seq;  /* columns of the device table */
     int32_t *device_block_table; /* [max_batch][max_blocks_per_seq], or NULL (host bookkeeping only) */
     int32_t *device_positions;   /* [max_batch], or NULL */
+    int32_t *device_context_lens; /* optional [max_batch]: position + 1 of each row's step token (the
+                                     context_lens of a cottus_paged_decode after cottus_qkv_rope_append), or NULL */
 } cottus_decode_batch_desc;
 
 int cottus_decode_batch_create(const cottus_decode_batch_desc *desc, cottus_decode_batch **out);

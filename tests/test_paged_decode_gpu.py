@@ -98,6 +98,30 @@ SMALL = {
 }
 
 
+@pytest.mark.parametrize("name,out_dtype", [("llama3_8b", torch.float16), ("ragged_mha", torch.float32)])
+def test_replayed_from_a_cuda_graph(oracle, name, out_dtype):
+    """One launch captured in a CUDA graph and replayed with new queries: the
+    arrival counters of the cut pairs return to zero at the end of every
+    launch, so each replay (same launch tag) merges its pairs again.  Covers
+    the tensor-core kernel (fp16, G=4) and the SIMT kernel (G=1, fp32 out)."""
+    w = SMALL[name]()
+    t = W.device_tensors(w, DEV)
+    out = torch.empty(t["query"].shape, dtype=out_dtype, device=DEV)
+    run(w, t, out=out)  # outside the capture: the cached workspace is sized here
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        cb.paged_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], num_kv_heads=w.Hkv,
+                        head_dim=w.D, block_size=w.bs, num_layers=w.L, layer=w.layer, out=out,
+                        num_physical_blocks=w.num_blocks)
+    gen = torch.Generator().manual_seed(31)
+    for _ in range(3):
+        t["query"].copy_(torch.randn(tuple(t["query"].shape), generator=gen).to(t["query"].dtype))
+        g.replay()
+        torch.cuda.synchronize()
+        assert max_abs(out, oracle_outputs(oracle, w, t, range(w.B))) <= tol_for(out_dtype)
+    del g
+
+
 @pytest.mark.parametrize("name", sorted(SMALL))
 def test_workload_vs_oracle(oracle, name):
     w = SMALL[name]()
