@@ -205,7 +205,9 @@ int cottus_rope_append_decode(const cottus_decode_step_params *p, cottus_stream_
 
 /* ------------------------------------------------------------------------
  * The step before attention, fused: QKV projection of each sequence's new
- * token, RoPE on q and k, and the KV append, in one kernel.  Replaces
+ * token, RoPE on q and k, and the KV append, in one call (a tensor-core
+ * projection kernel writing split partials to the workspace, then an
+ * epilogue kernel; stream-ordered, no host synchronisation).  Replaces
  * generic_transformer.cpp:169-284 per layer and token (gemmCUDA x3 =
  * cuBLAS SGEMM, compute_primitives_cuda.cu:30-55; ropeCUDA x2; the host
  * truncating encode and scatter).  Weights and activations are fp16 with
@@ -241,7 +243,8 @@ typedef struct {
     void *query_out;            /* [batch][num_heads][head_dim] rotated query */
     int32_t query_out_dtype;    /* enum cottus_dtype */
     float *qkv_out;             /* optional [batch][rows] fp32 projections before rotation */
-    void *workspace;            /* cottus_qkv_rope_append_workspace_size() bytes, 16-B aligned, any contents */
+    void *workspace;            /* cottus_qkv_rope_append_workspace_size() bytes, 16-B aligned, any contents
+                                   (not a buffer that cottus_paged_decode relies on: it is overwritten) */
     size_t workspace_bytes;
     uint32_t *status;           /* optional device word */
 } cottus_qkv_params;
@@ -267,7 +270,8 @@ typedef struct {
     const float *residual;  /* [batch][out_features] fp32 (may equal out when out_dtype is fp32) */
     void *out;              /* [batch][out_features], out_dtype */
     int32_t out_dtype;      /* enum cottus_dtype */
-    void *workspace;        /* cottus_o_proj_residual_workspace_size() bytes, 16-B aligned, any contents */
+    void *workspace;        /* cottus_o_proj_residual_workspace_size() bytes, 16-B aligned, any contents
+                               (overwritten; not a decode workspace) */
     size_t workspace_bytes;
     uint32_t *status;       /* optional device word */
 } cottus_o_proj_params;
