@@ -174,17 +174,18 @@ def run_reference(args, rank, world):
     import torch
     if world > 1 and rank != 0:
         return
-    if args.config in ("qkv_llama3_8b", "oproj_llama3_8b"):
-        qkv = args.config == "qkv_llama3_8b"
-        budget = min(2.0, 60.0 / max(args.steps + args.warmup, 1))
+    if args.config in ("qkv_llama3_8b", "oproj_llama3_8b", "attn_block_llama3_8b"):
+        fn, metric = {"qkv_llama3_8b": (qkv_reference_rate, "fused QKV+RoPE+append tokens/s"),
+                      "oproj_llama3_8b": (oproj_reference_rate, "O-projection+residual tokens/s"),
+                      "attn_block_llama3_8b": (attn_reference_rate, "attention block tokens/s")}[args.config]
+        budget = min(3.0 if fn is attn_reference_rate else 2.0, 60.0 / max(args.steps + args.warmup, 1))
         rates, sample, threads = [], "", 1
         t0 = time.perf_counter()
         for i in range(args.warmup + args.steps):
-            r, threads, sample = (qkv_reference_rate if qkv else oproj_reference_rate)(target_s=budget)
+            r, threads, sample = fn(target_s=budget)
             if i >= args.warmup:
                 rates.append(r)
         v = float(np.mean(rates))
-        metric = "fused QKV+RoPE+append tokens/s" if qkv else "O-projection+residual tokens/s"
         print(json.dumps({"metric": metric, "value": v, "unit": "tokens/s", "n_gpus": world,
                           "steps": args.steps, "warmup": args.warmup,
                           "ms_per_step": (time.perf_counter() - t0) / max(args.steps + args.warmup, 1) * 1e3,
@@ -538,6 +539,131 @@ def oproj_reference_rate(target_s=6.0):
     return done / el, threads, f"{done} tokens x 1 layer ({el:.1f} s wall, {threads} threads)"
 
 
+ATTN = dict(hidden=4096, H=32, Hkv=8, D=128, B=64, ctx=2048, layers=4, bs=16)  # Llama-3-8B, batch 64
+
+
+def run_attn_block(args, rank, world, local):
+    """The attention half of one decoder layer per step, for 64 sequences at
+    context 2048 (Llama-3-8B shape): QKV projection + RoPE + KV append
+    (cottus_qkv_rope_append), paged decode attention over the 2048 tokens
+    (cottus_paged_decode), O-projection + residual (cottus_o_proj_residual).
+    Four layers' weights (336 MB) and KV (2.1 GB) cycled; the three launches
+    of a step chained by programmatic dependent launch, replayed as a CUDA
+    graph of one step per layer.  Replicas per GPU (weak scaling)."""
+    import torch
+    import torch.distributed as dist
+    import cottus_b200 as cb
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    A = ATTN
+    H, Hkv, D, B, L, bs = A["H"], A["Hkv"], A["D"], A["B"], A["layers"], A["bs"]
+    N, HD = (H + 2 * Hkv) * D, H * D
+    g = torch.Generator(device="cpu").manual_seed(13)
+    x = torch.randn((B, A["hidden"]), generator=g).half().to(dev)
+    wq = [(torch.randn((N, A["hidden"]), generator=g) / A["hidden"] ** 0.5).half().to(dev) for _ in range(L)]
+    wo = [(torch.randn((A["hidden"], HD), generator=g) / HD ** 0.5).half().to(dev) for _ in range(L)]
+    resid = torch.randn((B, A["hidden"]), generator=g).to(dev)
+    pages = A["ctx"] // bs
+    nb = B * pages
+    gd = torch.Generator(device=dev).manual_seed(14)
+    pool = torch.randn(nb * 2 * L * bs * Hkv * D, generator=gd, device=dev).half().view(torch.int16)
+    table = torch.randperm(nb, generator=g).int().view(B, pages).to(dev)
+    pos = torch.full((B,), A["ctx"] - 1, dtype=torch.int32, device=dev)
+    ctx_lens = pos + 1
+    tab = cb.rope_cos_sin_table(A["ctx"], D).to(dev)
+    q = torch.empty((B, H, D), dtype=torch.float16, device=dev)
+    att = torch.empty((B, H, D), dtype=torch.float16, device=dev)
+
+    def step(i, xx=x):
+        layer = i % L
+        cb.qkv_rope_append(xx, wq[layer], pos, tab, pool, table, num_heads=H, num_kv_heads=Hkv, head_dim=D,
+                           block_size=bs, num_layers=L, layer=layer, num_physical_blocks=nb, query_out=q)
+        cb.paged_decode(q, pool, table, ctx_lens, num_kv_heads=Hkv, head_dim=D, block_size=bs, num_layers=L,
+                        layer=layer, out=att, num_physical_blocks=nb)
+        cb.o_proj_residual(att.view(B, HD), wo[layer], resid, out=resid)
+
+    gr = graph_of_steps(step, L, dev)
+    reps = max(args.steps // L, 1)
+    args_g = argparse.Namespace(**{**vars(args), "steps": reps, "warmup": max(args.warmup // L, 3)})
+    ms, clocks = timed_steps(lambda i: gr.replay(), args_g, dev, world, local)
+    ms /= L
+    steps_timed = reps * L
+    # end to end: the normalised hidden state from pinned host memory, the residual stream back
+    e_ms = e2e_steps(step, x, resid, args, dev, world)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        r, cores, sample = attn_reference_rate(target_s=9.0)
+        cpu = {"value": r, "unit": "tokens/s", "cores": cores, "kind": "reference", "sample": sample}
+    if world > 1:
+        dist.barrier()
+        if rank != 0:
+            dist.destroy_process_group()
+            return
+    peak, peak_kind = peaks()
+    wbytes = (N + A["hidden"]) * A["hidden"] * 2
+    kv_read = B * A["ctx"] * 2 * Hkv * D * 2
+    alg = (wbytes + kv_read + x.numel() * 2 + 2 * q.numel() * 2 + att.numel() * 2 + 2 * resid.numel() * 4 +
+           B * 2 * Hkv * D * 2 + table.numel() * 4)
+    line = {
+        "metric": "attention block tokens/s", "value": world * B / (ms * 1e-3), "unit": "tokens/s",
+        "n_gpus": world, "steps": steps_timed, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16 x f16 -> f32",
+        "data": "synthetic: seeded N(0,1) activations, KV and residual, N(0, 1/in) fp16 weights",
+        "config": {"workload": f"attn_block_llama3_8b: hidden {A['hidden']}, H{H}/Hkv{Hkv}/D{D}, batch {B}, "
+                               f"context {A['ctx']}, one of {L} layers per step (QKV+RoPE+append, paged decode, "
+                               f"O-proj+residual)",
+                   "l2": f"{L} layers' weights ({L * wbytes / 1e6:.0f} MB) and KV ({L * kv_read / 1e9:.1f} GB) "
+                         "cycled, > 126 MB L2",
+                   "parallelism": f"replicas on {world} GPU(s), no collective"},
+        "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                     "frac": alg / (ms * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
+                     "kernel": "qkv_proj_kernel + qkv_finish_kernel + decode_mma_kernel + qkv_proj_kernel + "
+                               "oproj_finish_kernel per step (CUDA graph of 4 layers' steps)",
+                     "kernel_ms": ms, "algorithmic_bytes": alg},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * B / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 2,
+                "d2h_bytes_per_step": resid.numel() * 4, "ms_per_step": e_ms,
+                "api": "cottus_qkv_rope_append + cottus_paged_decode + cottus_o_proj_residual (C ABI via ctypes)"},
+        "gpu_launches": 5 * steps_timed, "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+    del gr
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def attn_reference_rate(target_s=9.0):
+    """The reference's CPU path of the attention block for one token and one
+    layer: gemmCPU x3 + ropeCPU (QKV), pagedAttentionCPU over 2048 tokens,
+    gemmCPU with wo + residualAddCPU, each phase timed over all host threads;
+    the phases run one after the other, so tokens/s = 1 / (sum of the
+    phases' seconds per token).  Returns (tokens/s, threads, sample)."""
+    import torch
+    from cottus_b200 import workloads as W
+
+    r_q, threads, _ = qkv_reference_rate(target_s=target_s / 3)
+    r_o, _, _ = oproj_reference_rate(target_s=target_s / 3)
+    w = W.llama3_8b(seed=9, B=threads, context=ATTN["ctx"])
+    t = W.device_tensors(w, "cpu")
+    rb = ReferenceBatch(w, t)
+    n, reps, t0 = len(rb.ctx), 0, time.perf_counter()
+    while True:
+        rb.run(n)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= target_s / 3:
+            break
+    r_a = n * reps / el
+    del t, torch
+    r = 1.0 / (1.0 / r_q + 1.0 / r_a + 1.0 / r_o)
+    return r, threads, (f"per phase, all {threads} threads: QKV {r_q:.0f}, attention over {ATTN['ctx']} tokens "
+                        f"{r_a:.0f}, O-proj {r_o:.0f} tokens/s")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -546,7 +672,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="llama3_8b",
                     choices=["tinyllama_f32", "llama3_8b", "ragged_mha", "long_ctx_70b", "fused_tinyllama",
-                             "qkv_llama3_8b", "oproj_llama3_8b"])
+                             "qkv_llama3_8b", "oproj_llama3_8b", "attn_block_llama3_8b"])
     ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -570,6 +696,9 @@ def main():
         return
     if args.config == "oproj_llama3_8b":
         run_oproj(args, rank, world, local)
+        return
+    if args.config == "attn_block_llama3_8b":
+        run_attn_block(args, rank, world, local)
         return
 
     import cottus_b200 as cb
