@@ -105,11 +105,11 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D, G, QSPLIT>())
     }
     __syncthreads();
 
-    grid_dependency_wait();
-    grid_dependents_launch();
-
     const long long W = (long long)gridDim.x * kNW;
     const long long w = (long long)blockIdx.x * kNW + warp;
+    warm_first_pages<ROPE>(a, &kv_map, w, W, lane, REG, 64);
+    grid_dependency_wait();
+    grid_dependents_launch();
     const WorkerPlan pl = plan_worker<D, ROPE>(a, w, W, lane);
     const long long U = pl.U, chunk = pl.chunk;
     const long long NC = (U + chunk - 1) / chunk;

@@ -367,6 +367,42 @@ __device__ __forceinline__ long long grab_chunk(const TmaArgs& a, long long W, l
     return __shfl_sync(0xffffffffu, id, 0);
 }
 
+// Pages of a worker's static chunk warmed in L2 before the wait for the
+// preceding kernel.
+constexpr int kWarmPages = 2;
+
+// L2 prefetch (TMA, nothing written) of the first kWarmPages pages of this
+// worker's static chunk, issued before griddepcontrol.wait so that a launch
+// made resident during the preceding kernel's tail streams its first pages
+// meanwhile.  The cursor is located as plan_worker locates it, from lengths
+// and table entries that the preceding kernel may still be writing: a stale
+// read only warms the wrong lines (block ids are range-checked, the tensor
+// map bounds the box, and the real loads come after the wait; L2 is the
+// point of coherence, so nothing stale can be read from it).
+template <bool ROPE>
+__device__ __forceinline__ void warm_first_pages(const TmaArgs& a, const CUtensorMap* map, long long w,
+                                                 long long W, int lane, int boxes, int box_elems) {
+    constexpr unsigned FULL = 0xffffffffu;
+    if (kWarmPages == 0) return;
+    long long total = 0;
+    for (int b = lane; b < a.B; b += 32) total += seq_pages<ROPE>(a, b);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(FULL, total, o);
+    const long long U = total * a.Hkv;
+    const long long chunk = max((U + W * kChunksPerWorker - 1) / (W * kChunksPerWorker), (long long)kMinChunk);
+    const long long u0 = w * chunk;
+    if (u0 >= U) return;
+    Cursor c = locate_unit<ROPE>(a, u0, lane);
+    if (lane != 0 || c.b < 0) return;
+    const int n = (int)min((long long)kWarmPages, min(chunk, U - u0));
+    for (int k = 0; k < n; ++k) {
+        const int blk = a.bt[(long long)c.b * a.maxb + c.p];
+        if (blk >= 0 && (long long)blk < a.num_blocks)
+            for (int r = 0; r < boxes; ++r) tma_prefetch_l2_3d(map, r * box_elems, c.h, (blk * a.L + a.layer) * (2 * kBS));
+        cursor_next<ROPE>(c, a);
+    }
+}
+
 // Called by a worker after it stored its partial of a cut (sequence, kv
 // head) pair whose units are [ps, ps + np).  Worker wk owns units
 // [wk*chunk, (wk+1)*chunk), so the pair's partials belong to workers
@@ -491,12 +527,12 @@ __global__ void __launch_bounds__(kNW * 32)
     }
     __syncthreads();
 
-    grid_dependency_wait();
-    grid_dependents_launch();
-
     // ---- work: static chunk w, then chunks from the queue ----------------
     const long long W = (long long)gridDim.x * kNW;
     const long long w = (long long)blockIdx.x * kNW + warp;
+    warm_first_pages<ROPE>(a, &kv_map, w, W, lane, 1, 0);
+    grid_dependency_wait();
+    grid_dependents_launch();
     const WorkerPlan pl = plan_worker<D, ROPE>(a, w, W, lane);
     const long long U = pl.U, chunk = pl.chunk;
     const long long NC = (U + chunk - 1) / chunk;
