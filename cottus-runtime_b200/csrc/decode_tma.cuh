@@ -259,6 +259,42 @@ struct WorkerPlan {
     Cursor cur;
 };
 
+// The sequence that holds unit u, from per-lane page counts: pg[i] of lane
+// l is the page count of sequence 32 i + l.  Returns the sequence (-1 if no
+// sequence holds u), the units before it, and the register slot and lane
+// it came from (for reading other per-sequence values of the same snapshot).
+struct CachedHit {
+    int b, i, src;
+    long long excl;
+};
+__device__ __forceinline__ CachedHit locate_cached(const int (&pg)[kPlanRegs], long long u, int Hkv, int lane) {
+    constexpr unsigned FULL = 0xffffffffu;
+    CachedHit h = {-1, 0, 0, 0};
+    long long base = 0;
+#pragma unroll
+    for (int i = 0; i < kPlanRegs; ++i) {
+        if (h.b >= 0) break;
+        const long long units = (long long)pg[i] * Hkv;
+        long long incl = units;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const long long t = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += t;
+        }
+        incl += base;
+        const long long excl = incl - units;
+        const unsigned hit = __ballot_sync(FULL, units > 0 && excl <= u && u < incl);
+        if (hit) {
+            h.src = __ffs(hit) - 1;
+            h.i = i;
+            h.b = 32 * i + h.src;
+            h.excl = __shfl_sync(FULL, excl, h.src);
+        }
+        base = __shfl_sync(FULL, incl, 31);
+    }
+    return h;
+}
+
 template <int D, bool ROPE>
 __device__ __forceinline__ WorkerPlan plan_worker(const TmaArgs& a, long long w, long long W, int lane) {
     constexpr unsigned FULL = 0xffffffffu;
@@ -315,31 +351,18 @@ __device__ __forceinline__ WorkerPlan plan_worker(const TmaArgs& a, long long w,
     }
     if (pl.u0 >= pl.u1) return pl;
     // locate u0 from the cached page counts
-    long long base = 0;
-    int fb = -1, fnp = 0, fn = 0;
-    long long fex = 0;
+    const CachedHit hit = locate_cached(pg, pl.u0, a.Hkv, lane);
+    int fnp = 0, fn = 0;
 #pragma unroll
-    for (int i = 0; i < kPlanRegs; ++i) {
-        if (fb >= 0) break;
-        const long long units = (long long)pg[i] * a.Hkv;
-        long long incl = units;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const long long t = __shfl_up_sync(FULL, incl, o);
-            if (lane >= o) incl += t;
+    for (int i = 0; i < kPlanRegs; ++i) {  // register arrays are indexed with constants only
+        const int np_i = __shfl_sync(FULL, pg[i], hit.src), n_i = __shfl_sync(FULL, cx[i], hit.src);
+        if (i == hit.i) {
+            fnp = np_i;
+            fn = n_i;
         }
-        incl += base;
-        const long long excl = incl - units;
-        const unsigned hit = __ballot_sync(FULL, units > 0 && excl <= pl.u0 && pl.u0 < incl);
-        if (hit) {
-            const int src = __ffs(hit) - 1;
-            fb = 32 * i + src;
-            fex = __shfl_sync(FULL, excl, src);
-            fnp = __shfl_sync(FULL, pg[i], src);
-            fn = __shfl_sync(FULL, cx[i], src);
-        }
-        base = __shfl_sync(FULL, incl, 31);
     }
+    const int fb = hit.b;
+    const long long fex = hit.excl;
     const long long r = pl.u0 - fex;
     pl.cur.b = fb;
     pl.cur.np = fnp;
@@ -371,35 +394,53 @@ __device__ __forceinline__ long long grab_chunk(const TmaArgs& a, long long W, l
 // preceding kernel.
 constexpr int kWarmPages = 2;
 
-// L2 prefetch (TMA, nothing written) of the first kWarmPages pages of this
+// L2 prefetch (TMA, nothing written) of the first pages (at most
+// kWarmPages, within its first (sequence, kv head) segment) of this
 // worker's static chunk, issued before griddepcontrol.wait so that a launch
 // made resident during the preceding kernel's tail streams its first pages
-// meanwhile.  The cursor is located as plan_worker locates it, from lengths
-// and table entries that the preceding kernel may still be writing: a stale
-// read only warms the wrong lines (block ids are range-checked, the tensor
-// map bounds the box, and the real loads come after the wait; L2 is the
-// point of coherence, so nothing stale can be read from it).
+// meanwhile.  The chunk is located as plan_worker locates it, from one
+// snapshot of the lengths that the preceding kernel may still be writing:
+// a stale snapshot only warms the wrong lines (every index is checked
+// against the snapshot and the table's bounds, block ids against the pool,
+// the tensor map bounds the box, and the real loads come after the wait;
+// L2 is the point of coherence, so nothing stale can be read from it).
+// Batches beyond kPlanRegs * 32 sequences are not warmed.
 template <bool ROPE>
 __device__ __forceinline__ void warm_first_pages(const TmaArgs& a, const CUtensorMap* map, long long w,
                                                  long long W, int lane, int boxes, int box_elems) {
     constexpr unsigned FULL = 0xffffffffu;
-    if (kWarmPages == 0) return;
+    if (kWarmPages == 0 || a.B > 32 * kPlanRegs) return;
+    int pg[kPlanRegs];
     long long total = 0;
-    for (int b = lane; b < a.B; b += 32) total += seq_pages<ROPE>(a, b);
+#pragma unroll
+    for (int i = 0; i < kPlanRegs; ++i) {
+        const int b = lane + 32 * i;
+        pg[i] = b < a.B ? seq_pages<ROPE>(a, b) : 0;
+        total += pg[i];
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(FULL, total, o);
     const long long U = total * a.Hkv;
     const long long chunk = max((U + W * kChunksPerWorker - 1) / (W * kChunksPerWorker), (long long)kMinChunk);
     const long long u0 = w * chunk;
     if (u0 >= U) return;
-    Cursor c = locate_unit<ROPE>(a, u0, lane);
-    if (lane != 0 || c.b < 0) return;
-    const int n = (int)min((long long)kWarmPages, min(chunk, U - u0));
-    for (int k = 0; k < n; ++k) {
-        const int blk = a.bt[(long long)c.b * a.maxb + c.p];
+    const CachedHit hit = locate_cached(pg, u0, a.Hkv, lane);
+    int np = 0;
+#pragma unroll
+    for (int i = 0; i < kPlanRegs; ++i) {
+        const int np_i = __shfl_sync(FULL, pg[i], hit.src);
+        if (i == hit.i) np = np_i;
+    }
+    if (lane != 0 || hit.b < 0 || hit.b >= a.B || np <= 0) return;
+    const long long r = u0 - hit.excl;
+    const int h = (int)(r / np);
+    int p = (int)(r % np);
+    if (h >= a.Hkv) return;
+    const int pend = (int)min((long long)np, (long long)p + min((long long)kWarmPages, U - u0));
+    for (; p < pend && p < a.maxb; ++p) {
+        const int blk = a.bt[(long long)hit.b * a.maxb + p];
         if (blk >= 0 && (long long)blk < a.num_blocks)
-            for (int r = 0; r < boxes; ++r) tma_prefetch_l2_3d(map, r * box_elems, c.h, (blk * a.L + a.layer) * (2 * kBS));
-        cursor_next<ROPE>(c, a);
+            for (int q = 0; q < boxes; ++q) tma_prefetch_l2_3d(map, q * box_elems, h, (blk * a.L + a.layer) * (2 * kBS));
     }
 }
 
