@@ -282,26 +282,61 @@ def graph_of_steps(step, n, dev):
     return g
 
 
-def e2e_steps(step, x, y, args, dev, world):
-    """Each step: x's values from pinned host memory, step(i, device copy), y
-    read back into pinned host memory; ms per step between CUDA events, max over ranks."""
+def pipelined_e2e(call, host_in, out, args, dev, world):
+    """End to end through the public API: every step uploads its inputs from
+    pinned host memory (host_in), runs call(i, device_inputs, device_out) and
+    reads device_out back into pinned host memory.  Two buffer sets and two
+    copy streams pipeline the steps, as a serving loop would: the uploads of
+    step i+1 and the read-back of step i-1 run on the copy engines while the
+    kernels of step i run.  Returns ms per step between CUDA events on the
+    compute stream (max over ranks)."""
     import torch
     stream = torch.cuda.current_stream(dev)
-    hx = x.cpu().pin_memory()
-    hy = torch.empty(y.shape, dtype=y.dtype).pin_memory()
-    dx = torch.empty_like(x)
+    slots = [dict(ins=[torch.empty(h.shape, dtype=h.dtype, device=dev) for h in host_in], out=out.clone(),
+                  hout=torch.empty(out.shape, dtype=out.dtype).pin_memory(),
+                  up=torch.cuda.Event(), ran=torch.cuda.Event(), down=torch.cuda.Event())
+             for _ in range(2)]
+    up_s, down_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def upload(i):
+        sl = slots[i % 2]
+        with torch.cuda.stream(up_s):
+            if i >= 2:
+                up_s.wait_event(sl["ran"])  # step i-2 has read this slot's inputs
+            for d, h in zip(sl["ins"], host_in):
+                d.copy_(h, non_blocking=True)
+            sl["up"].record(up_s)
+
+    def run(i):
+        sl = slots[i % 2]
+        stream.wait_event(sl["up"])
+        if i >= 2:
+            stream.wait_event(sl["down"])  # step i-2's output has been read back
+        call(i, sl["ins"], sl["out"])
+        sl["ran"].record(stream)
+        with torch.cuda.stream(down_s):
+            down_s.wait_event(sl["ran"])
+            sl["hout"].copy_(sl["out"], non_blocking=True)
+            sl["down"].record(down_s)
+
+    def steps(n):
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload(i + 1)
+            run(i)
+        stream.wait_event(slots[(n - 1) % 2]["down"])
+
     n_e2e = max(min(args.steps // 5, 2000), 10)
-    for i in range(3):
-        dx.copy_(hx, non_blocking=True)
-        step(i, dx)
-        hy.copy_(y, non_blocking=True)
+    steps(5)
     torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
-    for i in range(n_e2e):
-        dx.copy_(hx, non_blocking=True)
-        step(i, dx)
-        hy.copy_(y, non_blocking=True)
+    up_s.wait_event(a)
+    steps(n_e2e)
     b.record(stream)
     torch.cuda.synchronize(dev)
     return max_over_ranks(a.elapsed_time(b) / n_e2e, dev, world)
@@ -367,7 +402,9 @@ def run_qkv(args, rank, world, local):
     ms /= q["layers"]
     steps_timed = reps * q["layers"]
     # end to end: the step's activations from pinned host memory, the rotated query back
-    e_ms = e2e_steps(step, x, qout, args, dev, world)
+    e_ms = pipelined_e2e(lambda i, ins, o: cb.qkv_rope_append(ins[0], ws[i % q["layers"]], pos, tab, pool, table,
+                                                              layer=i % q["layers"], **dict(kw, query_out=o)),
+                         [x.cpu().pin_memory()], qout, args, dev, world)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r, cores, sample = qkv_reference_rate(target_s=6.0)
@@ -396,7 +433,7 @@ def run_qkv(args, rank, world, local):
         "cpu_baseline": cpu,
         "e2e": {"value": world * q["B"] / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": qout.numel() * 2, "ms_per_step": e_ms,
-                "api": "cottus_qkv_rope_append (C ABI via ctypes)"},
+                "api": "cottus_qkv_rope_append (C ABI via ctypes)", "pipelining": "two buffer sets, two copy streams"},
         "gpu_launches": 2 * steps_timed, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -471,7 +508,9 @@ def run_oproj(args, rank, world, local):
     ms /= o["layers"]
     steps_timed = reps * o["layers"]
     # end to end: the attention output from pinned host memory, the residual stream back
-    e_ms = e2e_steps(step, x, resid, args, dev, world)
+    o_layers = o["layers"]
+    e_ms = pipelined_e2e(lambda i, ins, o: cb.o_proj_residual(ins[0], ws[i % o_layers], o, out=o),
+                         [x.cpu().pin_memory()], resid, args, dev, world)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r, cores, sample = oproj_reference_rate(target_s=6.0)
@@ -501,7 +540,7 @@ def run_oproj(args, rank, world, local):
         "cpu_baseline": cpu,
         "e2e": {"value": world * o["B"] / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": resid.numel() * 4, "ms_per_step": e_ms,
-                "api": "cottus_o_proj_residual (C ABI via ctypes)"},
+                "api": "cottus_o_proj_residual (C ABI via ctypes)", "pipelining": "two buffer sets, two copy streams"},
         "gpu_launches": 2 * steps_timed, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
@@ -547,9 +586,9 @@ def run_attn_block(args, rank, world, local):
     context 2048 (Llama-3-8B shape): QKV projection + RoPE + KV append
     (cottus_qkv_rope_append), paged decode attention over the 2048 tokens
     (cottus_paged_decode), O-projection + residual (cottus_o_proj_residual).
-    Four layers' weights (336 MB) and KV (2.1 GB) cycled; the three launches
-    of a step chained by programmatic dependent launch, replayed as a CUDA
-    graph of one step per layer.  Replicas per GPU (weak scaling)."""
+    Four layers' weights (336 MB) and KV (2.1 GB) cycled; the three calls of
+    a step issued directly on the stream, their kernels chained by
+    programmatic dependent launch.  Replicas per GPU (weak scaling)."""
     import torch
     import torch.distributed as dist
     import cottus_b200 as cb
@@ -586,14 +625,19 @@ def run_attn_block(args, rank, world, local):
                         layer=layer, out=att, num_physical_blocks=nb)
         cb.o_proj_residual(att.view(B, HD), wo[layer], resid, out=resid)
 
-    gr = graph_of_steps(step, L, dev)
-    reps = max(args.steps // L, 1)
-    args_g = argparse.Namespace(**{**vars(args), "steps": reps, "warmup": max(args.warmup // L, 3)})
-    ms, clocks = timed_steps(lambda i: gr.replay(), args_g, dev, world, local)
-    ms /= L
-    steps_timed = reps * L
+    # direct launches: the host issues a step's three calls faster than the GPU runs them
+    ms, clocks = timed_steps(step, args, dev, world, local)
+    steps_timed = args.steps
     # end to end: the normalised hidden state from pinned host memory, the residual stream back
-    e_ms = e2e_steps(step, x, resid, args, dev, world)
+    def block(i, ins, o):
+        layer = i % L
+        cb.qkv_rope_append(ins[0], wq[layer], pos, tab, pool, table, num_heads=H, num_kv_heads=Hkv, head_dim=D,
+                           block_size=bs, num_layers=L, layer=layer, num_physical_blocks=nb, query_out=q)
+        cb.paged_decode(q, pool, table, ctx_lens, num_kv_heads=Hkv, head_dim=D, block_size=bs, num_layers=L,
+                        layer=layer, out=att, num_physical_blocks=nb)
+        cb.o_proj_residual(att.view(B, HD), wo[layer], o, out=o)
+
+    e_ms = pipelined_e2e(block, [x.cpu().pin_memory()], resid, args, dev, world)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         r, cores, sample = attn_reference_rate(target_s=9.0)
@@ -622,16 +666,16 @@ def run_attn_block(args, rank, world, local):
         "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
                      "frac": alg / (ms * 1e-3) / 1e9 / peak, "traffic": None, "peak_kind": peak_kind,
                      "kernel": "qkv_proj_kernel + qkv_finish_kernel + decode_mma_kernel + qkv_proj_kernel + "
-                               "oproj_finish_kernel per step (CUDA graph of 4 layers' steps)",
+                               "oproj_finish_kernel per step (direct launches, layers cycled)",
                      "kernel_ms": ms, "algorithmic_bytes": alg},
         "cpu_baseline": cpu,
         "e2e": {"value": world * B / (e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": x.numel() * 2,
                 "d2h_bytes_per_step": resid.numel() * 4, "ms_per_step": e_ms,
-                "api": "cottus_qkv_rope_append + cottus_paged_decode + cottus_o_proj_residual (C ABI via ctypes)"},
+                "api": "cottus_qkv_rope_append + cottus_paged_decode + cottus_o_proj_residual (C ABI via ctypes)",
+                "pipelining": "two buffer sets, two copy streams"},
         "gpu_launches": 5 * steps_timed, "clocks": clocks,
     }
     print(json.dumps(line), flush=True)
-    del gr
     if world > 1:
         dist.destroy_process_group()
 
@@ -811,69 +855,17 @@ def main():
     k_ms = float(np.mean([a.elapsed_time(b) for a, b in ka]))
 
     # end to end through the C ABI with host buffers: every step copies its query, table and lengths
-    # from pinned host memory and reads its output back into pinned host memory.  Two buffer sets
-    # and two copy streams pipeline the steps: the uploads of step i+1 and the read-back of step i-1
-    # run on the copy engines while the kernel of step i runs.
+    # from pinned host memory and reads its output back into pinned host memory (pipelined: the
+    # copies of neighbouring steps overlap each kernel)
     e2e = None
     if not args.no_e2e and not split and not w.fused:
-        hq = t["query"].cpu().pin_memory()
-        hbt = t["block_table"].cpu().pin_memory()
-        hctx = t["context_lens"].cpu().pin_memory()
-        slots = [dict(q=torch.empty_like(t["query"]), bt=torch.empty_like(t["block_table"]),
-                      ctx=torch.empty_like(t["context_lens"]), out=torch.empty_like(out),
-                      hout=torch.empty(out.shape, dtype=out.dtype).pin_memory(),
-                      up=torch.cuda.Event(), ran=torch.cuda.Event(), down=torch.cuda.Event())
-                 for _ in range(2)]
-        up_s, down_s = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-        n_e2e = max(min(args.steps // 5, 2000), 10)
-
-        def upload(i):
-            sl = slots[i % 2]
-            with torch.cuda.stream(up_s):
-                if i >= 2:
-                    up_s.wait_event(sl["ran"])  # step i-2 has read this slot's inputs
-                sl["q"].copy_(hq, non_blocking=True)
-                sl["bt"].copy_(hbt, non_blocking=True)
-                sl["ctx"].copy_(hctx, non_blocking=True)
-                sl["up"].record(up_s)
-
-        def run(i):
-            sl = slots[i % 2]
-            stream.wait_event(sl["up"])
-            if i >= 2:
-                stream.wait_event(sl["down"])  # step i-2's output has been read back
-            cb.paged_decode(sl["q"], t["kv_pool"], sl["bt"], sl["ctx"], num_kv_heads=w.Hkv, head_dim=w.D,
-                            block_size=w.bs, out=sl["out"], num_physical_blocks=wl.num_blocks)
-            sl["ran"].record(stream)
-            with torch.cuda.stream(down_s):
-                down_s.wait_event(sl["ran"])
-                sl["hout"].copy_(sl["out"], non_blocking=True)
-                sl["down"].record(down_s)
-
-        def e2e_run(n):
-            upload(0)
-            for i in range(n):
-                if i + 1 < n:
-                    upload(i + 1)
-                run(i)
-            stream.wait_event(slots[(n - 1) % 2]["down"])
-
-        e2e_run(5)
-        torch.cuda.synchronize(dev)
-        if world > 1:
-            dist.barrier()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        up_s.wait_event(a)
-        e2e_run(n_e2e)
-        b.record(stream)
-        torch.cuda.synchronize(dev)
-        e_ms = a.elapsed_time(b) / n_e2e
-        if world > 1:
-            tt = torch.tensor([e_ms], device=dev)
-            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-            e_ms = float(tt.item())
-        h2d = hq.numel() * hq.element_size() + hbt.numel() * 4 + hctx.numel() * 4
+        host_in = [t["query"].cpu().pin_memory(), t["block_table"].cpu().pin_memory(),
+                   t["context_lens"].cpu().pin_memory()]
+        e_ms = pipelined_e2e(lambda i, ins, o: cb.paged_decode(ins[0], t["kv_pool"], ins[1], ins[2],
+                                                               num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
+                                                               out=o, num_physical_blocks=wl.num_blocks),
+                             host_in, out, args, dev, world)
+        h2d = sum(h.numel() * h.element_size() for h in host_in)
         d2h = out.numel() * out.element_size()
         e2e = {"value": world * kv_bytes_rank / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "api": "cottus_paged_decode (C ABI via ctypes)",

@@ -249,9 +249,9 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
 // One thread per (token, row pair): the splits added in order, then RoPE,
 // the rotated query and the append.
 __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvArgs a) {
-    // the next projection may start streaming its weights while this runs;
-    // it waits for this grid before it touches the activations or partials
-    grid_dependents_launch();
+    // No early release of the next kernel: a decode or projection made
+    // resident while this short kernel runs measured slower than one
+    // launched at its completion.
     grid_dependency_wait();  // the partials of the projection kernel are complete
     const int pairs_all = a.N / 2;
     const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -310,8 +310,7 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvArgs a) {
 // in order, then the residual (generic_transformer.cpp:305-325: x = att . Wo,
 // then x = x + xb).
 __global__ void __launch_bounds__(256) oproj_finish_kernel(const QkvArgs a) {
-    grid_dependents_launch();
-    grid_dependency_wait();
+    grid_dependency_wait();  // (no early release of the next kernel, as in qkv_finish_kernel)
     const int pairs_all = a.N / 2;
     const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (idx >= (long long)a.B * pairs_all) return;
