@@ -115,9 +115,8 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
     // tile read neighbouring 128-byte pieces of the same weight rows
     const int nsteps = split < a.ksteps ? (a.ksteps - split + a.splits - 1) / a.splits : 0;
     const int npre = nsteps < kQStages ? nsteps : kQStages;
-    // the finish kernel may become resident now: it holds no shared memory
-    // and waits for this grid to complete before it reads anything
-    grid_dependents_launch();
+    // (the finish kernel is released at exit: releasing it at the start
+    // measured slower in a chained decode step)
 
     if (threadIdx.x == 0) {
         prefetch_tensormap(&wmap);
