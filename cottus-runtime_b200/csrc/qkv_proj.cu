@@ -115,8 +115,9 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
     // tile read neighbouring 128-byte pieces of the same weight rows
     const int nsteps = split < a.ksteps ? (a.ksteps - split + a.splits - 1) / a.splits : 0;
     const int npre = nsteps < kQStages ? nsteps : kQStages;
-    // (the finish kernel is released at exit: releasing it at the start
-    // measured slower in a chained decode step)
+    // (the finish kernel is released at exit: released at the start, with
+    // the finish kernels also releasing early, a chained decode step
+    // measured up to 28 us slower)
 
     if (threadIdx.x == 0) {
         prefetch_tensormap(&wmap);
@@ -248,9 +249,10 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
 // One thread per (token, row pair): the splits added in order, then RoPE,
 // the rotated query and the append.
 __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvArgs a) {
-    // No early release of the next kernel: a decode or projection made
-    // resident while this short kernel runs measured slower than one
-    // launched at its completion.
+    // the next kernel may become resident now and run its prologue (a
+    // projection prefetches its weights, a decode warms its first pages);
+    // it waits for this grid before it reads anything this one writes
+    grid_dependents_launch();
     grid_dependency_wait();  // the partials of the projection kernel are complete
     const int pairs_all = a.N / 2;
     const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -309,7 +311,8 @@ __global__ void __launch_bounds__(256) qkv_finish_kernel(const QkvArgs a) {
 // in order, then the residual (generic_transformer.cpp:305-325: x = att . Wo,
 // then x = x + xb).
 __global__ void __launch_bounds__(256) oproj_finish_kernel(const QkvArgs a) {
-    grid_dependency_wait();  // (no early release of the next kernel, as in qkv_finish_kernel)
+    grid_dependents_launch();  // (as in qkv_finish_kernel)
+    grid_dependency_wait();
     const int pairs_all = a.N / 2;
     const long long idx = blockIdx.x * (long long)blockDim.x + threadIdx.x;
     if (idx >= (long long)a.B * pairs_all) return;
