@@ -15,11 +15,13 @@
 //       its own accumulator columns needs no broadcast.
 //   O^T[D x 8 cols] += V^T[D x 16] . P^T[16 x 8]          (D/16 MMAs)
 //       A = V rows through ldmatrix.trans, B = the probabilities in fp16,
-//       transposed in registers with movmatrix.
-//
-// Used where the output is fp16, or fp32 LSE partials of a split context
-// (whose merged result is fp16): fp16 probabilities bound the relative error
-// of each weight by 2^-11.  fp32-output calls keep the SIMT kernel.
+//       transposed in registers with movmatrix.  fp16 probabilities bound
+//       the relative error of each weight by 2^-11: enough where the output
+//       is fp16, or fp32 LSE partials of a split context (whose merged
+//       result is fp16).  For fp32 outputs (PSPLIT) each probability is
+//       also split into fp16 hi + lo parts (hi = its fp16 rounding, lo = the
+//       fp16 rounding of the remainder), two MMAs per dim tile, so weights
+//       keep about 2^-22 relative accuracy, as with fp32 queries above.
 #pragma once
 
 #include "decode_tma.cuh"
@@ -69,16 +71,15 @@ constexpr size_t mma_smem_bytes() {
     return (size_t)kNW * RING * MmaCfg<D>::SLOT_BYTES + (size_t)kNW * RING * 8 + (size_t)kNW * RING * 4 + 1024;
 }
 
-// CTAs per SM the register budget is fitted to: three rings of pages per SM
-// keep more bytes in flight than two; the split-query and group-8 variants
-// need more registers and settle for two.
-template <int D, int G, bool QSPLIT>
-constexpr int mma_min_ctas() {
-    return (QSPLIT || G >= 8) ? 2 : 3;
-}
+// CTAs per SM the register budget is fitted to: two.  Three (168
+// registers) keep more pages in flight, but the launch then has 1.5x the
+// workers, so more (sequence, kv head) pairs are cut between workers and
+// merged at the end: measured on the Llama-3-8B shape (batch 64, context
+// 2048), 94.8 us per step with three against 90.5 us with two.
+constexpr int kMmaMinCtas = 2;
 
-template <int D, int G, int RING, bool ROPE, bool QSPLIT>
-__global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D, G, QSPLIT>())
+template <int D, int G, int RING, bool ROPE, bool QSPLIT, bool PSPLIT>
+__global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
     decode_mma_kernel(const __grid_constant__ CUtensorMap kv_map, const TmaArgs a) {
     using C = MmaCfg<D>;
     constexpr int KS = C::KSTEPS, REG = C::REGIONS, LW = D / 8;
@@ -363,6 +364,12 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D, G, QSPLIT>())
             l1 += p01 + p11;
             const uint32_t pb0 = movmatrix_trans(pack_h2(p00, p01));  // tokens 0-7
             const uint32_t pb1 = movmatrix_trans(pack_h2(p10, p11));  // tokens 8-15
+            uint32_t pl0 = 0u, pl1 = 0u;  // fp32 outputs: the remainders of the fp16 roundings
+            if constexpr (PSPLIT) {
+                const float2 h0 = unpack_h2(pack_h2(p00, p01)), h1 = unpack_h2(pack_h2(p10, p11));
+                pl0 = movmatrix_trans(pack_h2(p00 - h0.x, p01 - h0.y));
+                pl1 = movmatrix_trans(pack_h2(p10 - h1.x, p11 - h1.y));
+            }
 
             // ---- O^T += V^T . P^T --------------------------------------------------
             {
@@ -373,6 +380,7 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D, G, QSPLIT>())
                     uint32_t af[4];
                     ldsm_x4_t(sl_s + swz(j / 4, kBS + tok, (j % 4) * 2 + csel), af);
                     mma16816(o[j], af, pb0, pb1);
+                    if constexpr (PSPLIT) mma16816(o[j], af, pl0, pl1);
                 }
             }
             __syncwarp();
@@ -445,13 +453,13 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D, G, QSPLIT>())
     signal_done(a, lane, &cta_done);
 }
 
-template <int D, int G, int RING, bool ROPE, bool QSPLIT>
+template <int D, int G, int RING, bool ROPE, bool QSPLIT, bool PSPLIT>
 struct MmaLauncher {
     static int blocks_per_sm(int device) {
         static int cache[64] = {0};
         if (device < 0 || device >= 64) return 1;
         if (cache[device] == 0) {
-            auto kern = decode_mma_kernel<D, G, RING, ROPE, QSPLIT>;
+            auto kern = decode_mma_kernel<D, G, RING, ROPE, QSPLIT, PSPLIT>;
             const size_t smem = mma_smem_bytes<RING, D>();
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             int n = 0;
@@ -471,24 +479,23 @@ struct MmaLauncher {
         const CUtensorMap map = make_kv_tensor_map(d, true, &err);
         if (err != cudaSuccess) return err;
         TmaArgs a = make_tma_args(d, W, G, D);
-        return launch_pdl(decode_mma_kernel<D, G, RING, ROPE, QSPLIT>, (int)(W / kNW), mma_smem_bytes<RING, D>(), st,
+        return launch_pdl(decode_mma_kernel<D, G, RING, ROPE, QSPLIT, PSPLIT>, (int)(W / kNW), mma_smem_bytes<RING, D>(), st,
                           map, a);
     }
 };
 
-template <int D, int RING, bool ROPE, bool QSPLIT>
+template <int D, int RING, bool ROPE, bool QSPLIT, bool PSPLIT>
 cudaError_t dispatch_mma_g(const DecodeDesc& d, cudaStream_t st, bool workers_only, long long* W) {
     int dev = 0;
     cudaGetDevice(&dev);
-    switch (d.num_heads / d.num_kv_heads) {
-#define CB200_CASE(GG)                                                   \
-    case GG:                                                             \
-        if (workers_only) {                                              \
-            *W = MmaLauncher<D, GG, RING, ROPE, QSPLIT>::workers(dev);   \
-            return cudaSuccess;                                          \
-        }                                                                \
-        return MmaLauncher<D, GG, RING, ROPE, QSPLIT>::launch(d, st);
-        CB200_CASE(1)
+    switch (d.num_heads / d.num_kv_heads) {  // grouped queries only: MHA takes the SIMT kernel
+#define CB200_CASE(GG)                                                           \
+    case GG:                                                                     \
+        if (workers_only) {                                                      \
+            *W = MmaLauncher<D, GG, RING, ROPE, QSPLIT, PSPLIT>::workers(dev);   \
+            return cudaSuccess;                                                  \
+        }                                                                        \
+        return MmaLauncher<D, GG, RING, ROPE, QSPLIT, PSPLIT>::launch(d, st);
         CB200_CASE(2)
         CB200_CASE(4)
         CB200_CASE(8)
@@ -497,11 +504,18 @@ cudaError_t dispatch_mma_g(const DecodeDesc& d, cudaStream_t st, bool workers_on
     return cudaErrorInvalidValue;
 }
 
+// fp32 outputs (not LSE partials) split the probabilities too.
+template <int D, int RING, bool PSPLIT>
+cudaError_t dispatch_mma_p(const DecodeDesc& d, cudaStream_t st, bool workers_only, long long* W) {
+    if (d.rope) return dispatch_mma_g<D, RING, true, true, PSPLIT>(d, st, workers_only, W);
+    if (d.q_f16) return dispatch_mma_g<D, RING, false, false, PSPLIT>(d, st, workers_only, W);
+    return dispatch_mma_g<D, RING, false, true, PSPLIT>(d, st, workers_only, W);
+}
+
 template <int D, int RING>
 cudaError_t dispatch_mma(const DecodeDesc& d, cudaStream_t st, bool workers_only, long long* W) {
-    if (d.rope) return dispatch_mma_g<D, RING, true, true>(d, st, workers_only, W);
-    if (d.q_f16) return dispatch_mma_g<D, RING, false, false>(d, st, workers_only, W);
-    return dispatch_mma_g<D, RING, false, true>(d, st, workers_only, W);
+    if (!d.out_f16 && d.lse == nullptr) return dispatch_mma_p<D, RING, true>(d, st, workers_only, W);
+    return dispatch_mma_p<D, RING, false>(d, st, workers_only, W);
 }
 
 }  // namespace cb200

@@ -133,10 +133,8 @@ bool mma_supported(const DecodeDesc& d) {
     if (d.head_dim != 64 && d.head_dim != 128) return false;
     // without grouped queries the SIMT kernel is faster (measured: 6.1 vs
     // 5.5 TB/s on the MHA workload)
-    if (d.num_heads == d.num_kv_heads) return false;
-    // fp16 probabilities: only where the result is fp16, or fp32 LSE
-    // partials whose merge is (split contexts)
-    return d.out_f16 || d.lse != nullptr;
+    // (fp32 outputs split the probabilities into fp16 hi + lo parts)
+    return d.num_heads != d.num_kv_heads;
 }
 
 static size_t workers(const DecodeDesc& d) {
