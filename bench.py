@@ -197,7 +197,7 @@ def run_reference(args, rank, world):
               flush=True)
         return
     from cottus_b200 import workloads as W
-    w = build_workload(args.config, 0, args.batch)
+    w, config = decode_config(args, world)
     t = W.device_tensors(w, "cpu" if not torch.cuda.is_available() else "cuda")
     # each step is a bounded sample of the workload, sized from one timed sequence so that warm-up and
     # timed steps together take about a minute (a few at most): the first n whole sequences, or, where one
@@ -228,28 +228,40 @@ def run_reference(args, rank, world):
     v = float(np.mean(rates))
     line = {"metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": el / max(args.steps, 1) * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": describe(w), "kv": "fp16"}, "impl": "reference",
+            "scaling": "strong" if args.config == "long_ctx_70b" and world > 1 else "weak", "vs_baseline": None,
+            "dtype": "f32 (fp16 KV decoded to fp32; the reference's CPU arithmetic)", "data": "synthetic",
+            "config": config, "impl": "reference",
             "cpu_baseline": {"value": v, "unit": "GB/s", "cores": threads, "kind": "reference",
                              "sample": sample},
             "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
+def start_clocks(local):
+    """Starts the SM-clock sampler and lets it come up.  Called before the
+    warm-up steps, never between them and the timed region: a GPU left idle
+    for a fraction of a second runs its next steps slowly (measured: the
+    first step after a 0.3 s pause takes 130-210 us instead of 90 us)."""
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    return sampler
+
+
 def timed_steps(step, args, dev, world, local):
     """W untimed steps, then K steps between CUDA events on the current
-    stream with the SM clocks sampled; max over ranks.  Returns (ms per step, clocks)."""
+    stream with the SM clocks sampled; a synchronize and a barrier (no idle
+    pause) between the two; max over ranks.  Returns (ms per step, clocks)."""
     import torch
     import torch.distributed as dist
     stream = torch.cuda.current_stream(dev)
+    sampler = start_clocks(local)
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
+    torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
@@ -327,7 +339,7 @@ def pipelined_e2e(call, host_in, out, args, dev, world):
             run(i)
         stream.wait_event(slots[(n - 1) % 2]["down"])
 
-    n_e2e = max(min(args.steps // 5, 2000), 10)
+    n_e2e = min(max(args.steps, 20), 2000)
     steps(5)
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -708,6 +720,411 @@ def attn_reference_rate(target_s=9.0):
                         f"{r_a:.0f}, O-proj {r_o:.0f} tokens/s")
 
 
+# -- decode workloads ---------------------------------------------------------------------
+
+DTYPE_F16 = "f16 (fp16 Q, KV and O; fp16 probabilities on the tensor cores; fp32 accumulation)"
+DTYPE_F32 = "f32 out (fp16 KV; fp32 Q/O; fp32-accurate products as fp16 hi+lo pairs on the tensor cores; fp32 accumulation)"
+
+
+def l2_plan(kv_bytes):
+    """How a workload's steps avoid reading KV that an earlier step left in
+    L2.  KV of at least 2 x L2 per step: none needed.  Smaller KV: each step
+    is one layer of a pool of L layers and the steps cycle through the
+    layers, as a decode loop does, with L chosen so that a cycle covers
+    3 x L2; below 8 MB per layer that would take hundreds of layers, so the
+    step is timed alone after a 2 x L2 buffer is written instead.
+    Returns (layers, flush)."""
+    if kv_bytes >= 2 * L2_BYTES:
+        return 1, False
+    if kv_bytes >= 8 * 1024 * 1024:
+        return -(-3 * L2_BYTES // kv_bytes), False
+    return 1, True
+
+
+def l2_text(kv_bytes, layers, flush):
+    if flush:
+        return "L2 flushed between steps (2x L2 buffer written), each step timed alone"
+    if layers > 1:
+        return (f"{layers} layers' KV cycled ({layers * kv_bytes / 1e6:.0f} MB > 126 MB L2), one layer per step, "
+                "no flush")
+    return f"inputs larger than L2 ({kv_bytes / 1e6:.0f} MB KV per GPU vs 126 MB L2), no flush"
+
+
+def decode_kernel_name(w):
+    """The kernel cottus_paged_decode selects for this workload."""
+    mma = (w.H // w.Hkv) > 1 and w.D in (64, 128)
+    return ("decode_mma_kernel" if mma else "decode_tma_kernel") + (" (RoPE + append fused)" if w.fused else "")
+
+
+def decode_config(args, world):
+    """(workload, the JSON `config` object): the same in both arms."""
+    from cottus_b200 import workloads as W
+    w = build_workload(args.config, 0, args.batch)
+    split = args.config == "long_ctx_70b" and world > 1
+    per_gpu = w.kv_bytes() // world if split else w.kv_bytes()
+    layers, flush = l2_plan(per_gpu)
+    cfg = {"workload": describe(w), "kv": "fp16", "q_out": str(w.q_dtype).replace("torch.", ""),
+           "per_gpu_batch": w.B, "kv_bytes_per_step_per_gpu": per_gpu, "l2": l2_text(per_gpu, layers, flush),
+           "parallelism": ((f"split-KV over {world} GPUs, " +
+                            ("LSE partials read from peer memory over NVLink after a completion flag raised by the "
+                             "decode kernel" if args.exchange == "peer" else "NCCL all-gather of LSE partials"))
+                           if split else f"sequence-sharded over {world} GPU(s), no collective")}
+    del W
+    return w, cfg
+
+
+def run_decode(args, rank, world, local):
+    """The five decode workloads: one step = one cottus_paged_decode (or
+    cottus_rope_append_decode) launch over the batch; long_ctx_70b on N > 1
+    GPUs splits every sequence's pages over the ranks."""
+    import dataclasses
+
+    import torch
+    import torch.distributed as dist
+    import cottus_b200 as cb
+    from cottus_b200 import workloads as W
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    split = args.config == "long_ctx_70b" and world > 1
+    w, config = decode_config(args, world)
+    if not split:
+        w = build_workload(args.config, rank, args.batch)
+    if split:
+        wl = W.shard_long_context(w, rank, world)
+    else:
+        wl = w
+    kv_bytes_rank = wl.kv_bytes()
+    layers, flush = l2_plan(kv_bytes_rank)
+    if layers > 1:
+        w = dataclasses.replace(w, L=layers)
+        wl = w
+    if split:
+        t = W.device_tensors(wl, dev, pool_blocks=wl.meta["pool_range"])
+        t["block_table"] = torch.from_numpy(wl.block_table).to(dev)
+        t["context_lens"] = torch.from_numpy(wl.ctx).to(dev)
+    else:
+        t = W.device_tensors(wl, dev)
+    if w.fused:
+        t["cos_sin"] = cb.rope_cos_sin_table(int(w.positions.max()) + 1, w.D, w.theta).to(dev)
+
+    stream = torch.cuda.current_stream(dev)
+    out = torch.empty((w.B, w.H, w.D), dtype=w.out_dtype, device=dev)
+    part = torch.empty((w.B, w.H, w.D), dtype=torch.float32, device=dev)
+    lse = torch.empty((w.B, w.H), dtype=torch.float32, device=dev)
+    pool_snapshot = t["kv_pool"].clone() if w.fused else None  # the fused step appends; restore is not timed
+
+    exchange = None
+    if split:
+        from cottus_b200 import parallel
+        if args.exchange == "peer":
+            exchange = parallel.PeerExchange(w.B, w.H, w.D)
+    launches_per_step = 2 if split else 1
+
+    def step(i):
+        layer = i % w.L
+        if w.fused:
+            cb.rope_append_decode(t["query"], t["key"], t["value"], t["positions"], t["cos_sin"], t["kv_pool"],
+                                  t["block_table"], num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
+                                  num_layers=w.L, layer=layer, out=out)
+        elif split and exchange is not None:
+            # decode kernel (completion flagged to every rank) + combine kernel reading peers over NVLink
+            parallel.split_kv_decode_peer(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], exchange,
+                                          num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
+                                          num_physical_blocks=wl.num_blocks, out_dtype=w.out_dtype, out=out)
+        elif split:
+            parallel.split_kv_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"],
+                                     num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
+                                     num_physical_blocks=wl.num_blocks, out_dtype=w.out_dtype, part=part, lse=lse)
+        else:
+            cb.paged_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], num_kv_heads=w.Hkv,
+                            head_dim=w.D, block_size=w.bs, num_layers=w.L, layer=layer, out=out,
+                            num_physical_blocks=wl.num_blocks)
+
+    fbuf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
+
+    # W warm-up steps right before the K timed ones (no idle pause in between)
+    sampler = start_clocks(local)
+    for i in range(args.warmup):
+        if flush:
+            fbuf.fill_(float(i))
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    if flush:
+        # L2-resident working set: flush L2 between steps, time every step alone
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+        for i in range(args.steps):
+            fbuf.fill_(float(i))
+            evs[i][0].record(stream)
+            step(args.warmup + i)
+            evs[i][1].record(stream)
+        torch.cuda.synchronize(dev)
+        elapsed_ms = sum(a.elapsed_time(b) for a, b in evs)
+    else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(args.steps):
+            step(args.warmup + i)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        elapsed_ms = e0.elapsed_time(e1)
+    clocks = sampler.stop()
+    ms = max_over_ranks(elapsed_ms, dev, world) / args.steps
+
+    # the dominant kernel alone: one decode launch between each event pair
+    ka = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(50)]
+    for i, (a, b) in enumerate(ka):
+        if flush:
+            fbuf.fill_(1.0)
+        a.record(stream)
+        if w.fused:
+            step(i)
+        else:
+            cb.paged_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], num_kv_heads=w.Hkv,
+                            head_dim=w.D, block_size=w.bs, num_layers=w.L, layer=i % w.L,
+                            out=part if split else out, lse_out=lse if split else None,
+                            num_physical_blocks=wl.num_blocks)
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    k_ms = float(np.mean([a.elapsed_time(b) for a, b in ka]))
+
+    # end to end through the C ABI with host buffers: every step copies its inputs from pinned host
+    # memory and reads its output back into pinned host memory (pipelined: the copies of neighbouring
+    # steps overlap each kernel)
+    e2e = None
+    if not args.no_e2e and not split:
+        if w.fused:
+            host_in = [t["query"].cpu().pin_memory(), t["key"].cpu().pin_memory(), t["value"].cpu().pin_memory(),
+                       t["positions"].cpu().pin_memory(), t["block_table"].cpu().pin_memory()]
+
+            def call(i, ins, o):
+                cb.rope_append_decode(ins[0], ins[1], ins[2], ins[3], t["cos_sin"], t["kv_pool"], ins[4],
+                                      num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs, num_layers=w.L,
+                                      layer=i % w.L, out=o)
+            api = "cottus_rope_append_decode (C ABI via ctypes)"
+        else:
+            host_in = [t["query"].cpu().pin_memory(), t["block_table"].cpu().pin_memory(),
+                       t["context_lens"].cpu().pin_memory()]
+
+            def call(i, ins, o):
+                cb.paged_decode(ins[0], t["kv_pool"], ins[1], ins[2], num_kv_heads=w.Hkv, head_dim=w.D,
+                                block_size=w.bs, num_layers=w.L, layer=i % w.L, out=o,
+                                num_physical_blocks=wl.num_blocks)
+            api = "cottus_paged_decode (C ABI via ctypes)"
+        e_ms = pipelined_e2e(call, host_in, out, args, dev, world)
+        h2d = sum(h.numel() * h.element_size() for h in host_in)
+        d2h = out.numel() * out.element_size()
+        e2e = {"value": world * kv_bytes_rank / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "api": api,
+               "pipelining": "two buffer sets; uploads and read-backs on two copy streams overlap the kernels"}
+        if flush:
+            e2e["l2"] = "steps back to back, L2 not flushed between them"
+
+    if pool_snapshot is not None:
+        t["kv_pool"].copy_(pool_snapshot)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            wc = dataclasses.replace(w, L=1) if w.L > 1 else w
+            tc = W.device_tensors(wc, dev) if w.L > 1 else t
+            r, threads, sample = cpu_reference_rate(wc, tc, target_s=8.0,
+                                                    max_seqs=1 if w.name == "long_ctx_70b" else None)
+            cpu = {"value": r, "unit": "GB/s", "cores": threads, "kind": "reference", "sample": sample}
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {ex}"}
+
+    if exchange is not None:
+        exchange.close()  # collective: every rank is done with the peer buffers
+    del t, pool_snapshot, fbuf
+    torch.cuda.empty_cache()
+
+    extras = {}
+    if args.config == "llama3_8b" and not args.no_extras and args.batch is None:
+        extras["strong_scaling"] = strong_scaling_extra(args, rank, world, local)
+        extras["split_kv"] = split_kv_extra(args, rank, world, local)
+
+    if world > 1:
+        dist.barrier()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    peak, peak_kind = peaks()
+    total_kv = w.kv_bytes() if split else kv_bytes_rank * world
+    value = total_kv / (ms * 1e-3) / 1e9
+    alg = kv_bytes_rank + wl.io_bytes()
+    # launch duration for the roofline: where a step is one launch of the
+    # kernel, the timed region per launch (launches back to back, as a decode
+    # loop issues them); otherwise the kernel timed alone between events
+    kern_ms = ms if launches_per_step == 1 and not flush else k_ms
+    achieved = alg / (kern_ms * 1e-3) / 1e9
+    traffic = None
+    prof = ROOT / "profiles" / "traffic.json"
+    if prof.exists():
+        tr = json.loads(prof.read_text()).get(w.name)
+        traffic = tr.get("bytes_per_launch") if isinstance(tr, dict) else tr
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong" if split else "weak", "vs_baseline": None,
+        "dtype": DTYPE_F16 if w.out_dtype == torch.float16 else DTYPE_F32,
+        "data": "synthetic: seeded N(0,1) KV stored via the reference's truncating fp16 encoder",
+        "config": config,
+        "tokens_per_s": w.B * (1 if split else world) / (ms * 1e-3),
+        "pct_hbm_peak": value / world / peak * 100,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "peak_kind": peak_kind,
+                     "kernel": decode_kernel_name(w) + ((" + peer_combine_kernel" if args.exchange == "peer"
+                                                        else " + lse_combine_kernel") if split else "") +
+                     ": one decode launch per step",
+                     "kernel_ms": kern_ms, "kernel_ms_alone": k_ms, "algorithmic_bytes": alg},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
+    }
+    line.update(extras)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def device_ms(step, args, dev, world):
+    """W warm-up steps, then K steps between events on the current stream
+    (a synchronize and a barrier between the two); ms per step, max over ranks."""
+    import torch
+    import torch.distributed as dist
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        step(args.warmup + i)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    return max_over_ranks(e0.elapsed_time(e1), dev, world) / args.steps
+
+
+def strong_scaling_extra(args, rank, world, local):
+    """The default workload's fixed batch of 64 sequences partitioned across
+    the N ranks (64 / N sequences each, no collective), steps cycling
+    through enough layers' KV that no step reads L2-resident KV.  Total
+    work fixed as N grows."""
+    import dataclasses
+
+    import torch
+    import cottus_b200 as cb
+    from cottus_b200 import workloads as W
+
+    dev = torch.device("cuda", local)
+    B = 64
+    per = B // world
+    w = W.llama3_8b(seed=3000 + rank, B=per)
+    layers, _ = l2_plan(w.kv_bytes())
+    w = dataclasses.replace(w, L=layers)
+    t = W.device_tensors(w, dev)
+    out = torch.empty((w.B, w.H, w.D), dtype=w.out_dtype, device=dev)
+
+    def step(i):
+        cb.paged_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], num_kv_heads=w.Hkv,
+                        head_dim=w.D, block_size=w.bs, num_layers=w.L, layer=i % w.L, out=out,
+                        num_physical_blocks=w.num_blocks)
+
+    ms = device_ms(step, args, dev, world)
+    peak, _ = peaks()
+    total = B * 2048 * 2 * w.Hkv * w.D * 2
+    del t
+    torch.cuda.empty_cache()
+    return {"workload": f"llama3_8b batch {B} partitioned over {world} GPU(s): {per} sequences per GPU, "
+                        f"{l2_text(w.kv_bytes(), layers, False)}",
+            "scaling": "strong", "ms_per_step": ms, "GB_s": total / (ms * 1e-3) / 1e9,
+            "tokens_per_s": B / (ms * 1e-3), "frac_of_n_peaks": total / (ms * 1e-3) / 1e9 / (world * peak),
+            "gpu_launches": args.steps}
+
+
+def split_kv_extra(args, rank, world, local):
+    """The long-context workload (H64/Hkv8/D128, batch 8, context 131072,
+    4.3 GB of KV) with every sequence's pages split over the N ranks: per
+    step a decode of each rank's page range and the merge of the ranks'
+    partials, through peer memory (cottus_split_decode) and through NCCL.
+    Also times each rank's decode alone, and on rank 0 the un-split decode
+    on one GPU, so the line says where the N-GPU step loses to N-fold."""
+    import torch
+    import torch.distributed as dist
+    import cottus_b200 as cb
+    from cottus_b200 import parallel
+    from cottus_b200 import workloads as W
+
+    dev = torch.device("cuda", local)
+    w = W.long_ctx_70b(seed=4000)
+    out = torch.empty((w.B, w.H, w.D), dtype=torch.float16, device=dev)
+    peak, _ = peaks()
+    res = {"workload": f"long_ctx_70b: H{w.H}/Hkv{w.Hkv}/D{w.D}, batch {w.B}, context {int(w.ctx[0])}, "
+                       f"pages of every sequence split over {world} GPU(s)", "scaling": "strong"}
+    if world == 1:
+        t = W.device_tensors(w, dev)
+
+        def one(i):
+            cb.paged_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], num_kv_heads=w.Hkv,
+                            head_dim=w.D, block_size=w.bs, out=out, num_physical_blocks=w.num_blocks)
+        ms1 = device_ms(one, args, dev, world)
+        res.update({"ms_per_step": ms1, "GB_s": w.kv_bytes() / (ms1 * 1e-3) / 1e9,
+                    "frac_of_n_peaks": w.kv_bytes() / (ms1 * 1e-3) / 1e9 / peak, "ms_per_step_1gpu": ms1,
+                    "efficiency_vs_1gpu": 1.0, "gpu_launches": args.steps})
+        del t
+        torch.cuda.empty_cache()
+        return res
+    s = W.shard_long_context(w, rank, world)
+    t = W.device_tensors(s, dev, pool_blocks=s.meta["pool_range"])
+    bt, cl = torch.from_numpy(s.block_table).to(dev), torch.from_numpy(s.ctx).to(dev)
+    part = torch.empty((w.B, w.H, w.D), dtype=torch.float32, device=dev)
+    lse = torch.empty((w.B, w.H), dtype=torch.float32, device=dev)
+    kw = dict(num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs, num_physical_blocks=s.num_blocks)
+    ex = parallel.PeerExchange(w.B, w.H, w.D)
+    ms_peer = device_ms(lambda i: parallel.split_kv_decode_peer(t["query"], t["kv_pool"], bt, cl, ex,
+                                                                out_dtype=torch.float16, out=out, **kw),
+                        args, dev, world)
+    ex.close()
+    ms_nccl = device_ms(lambda i: parallel.split_kv_decode(t["query"], t["kv_pool"], bt, cl, out_dtype=torch.float16,
+                                                           part=part, lse=lse, **kw), args, dev, world)
+    ms_dec = device_ms(lambda i: cb.paged_decode(t["query"], t["kv_pool"], bt, cl, out=part, lse_out=lse, **kw),
+                       args, dev, world)
+    del t
+    torch.cuda.empty_cache()
+    ms1 = None
+    if rank == 0:
+        # the same workload un-split on this GPU alone (the other ranks wait at the barrier)
+        tf = W.device_tensors(w, dev)
+        one_args = argparse.Namespace(**{**vars(args)})
+
+        def one(i):
+            cb.paged_decode(tf["query"], tf["kv_pool"], tf["block_table"], tf["context_lens"], num_kv_heads=w.Hkv,
+                            head_dim=w.D, block_size=w.bs, out=out, num_physical_blocks=w.num_blocks)
+        ms1 = device_ms(one, one_args, dev, 1)
+        del tf
+        torch.cuda.empty_cache()
+    dist.barrier()
+    gb = w.kv_bytes() / (ms_peer * 1e-3) / 1e9
+    res.update({"exchange": "peer memory over NVLink (cottus_split_decode)", "ms_per_step": ms_peer,
+                "GB_s": gb, "frac_of_n_peaks": gb / (world * peak), "ms_per_step_nccl": ms_nccl,
+                "ms_decode_alone": ms_dec, "exchange_and_merge_ms": ms_peer - ms_dec, "ms_per_step_1gpu": ms1,
+                "efficiency_vs_1gpu": (ms1 / (world * ms_peer)) if ms1 else None,
+                "gpu_launches": 2 * args.steps})
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -720,13 +1137,12 @@ def main():
     ap.add_argument("--batch", type=int, default=None, help="override the batch size (profiling runs)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the strong-scaling and split-context lines added to the default workload's line")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="split-context partial exchange: peer memory over NVLink, or NCCL all-gather")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-
-    import torch
-    import torch.distributed as dist
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -735,204 +1151,8 @@ def main():
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
-    if args.config == "qkv_llama3_8b":
-        run_qkv(args, rank, world, local)
-        return
-    if args.config == "oproj_llama3_8b":
-        run_oproj(args, rank, world, local)
-        return
-    if args.config == "attn_block_llama3_8b":
-        run_attn_block(args, rank, world, local)
-        return
-
-    import cottus_b200 as cb
-    from cottus_b200 import workloads as W
-
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-
-    split = args.config == "long_ctx_70b" and world > 1
-    w = build_workload(args.config, 0 if split else rank, args.batch)
-    if split:
-        s = W.shard_long_context(w, rank, world)
-        t = W.device_tensors(s, dev, pool_blocks=s.meta["pool_range"])
-        t["block_table"] = torch.from_numpy(s.block_table).to(dev)
-        t["context_lens"] = torch.from_numpy(s.ctx).to(dev)
-        wl = s
-    else:
-        t = W.device_tensors(w, dev)
-        wl = w
-    if w.fused:
-        t["cos_sin"] = cb.rope_cos_sin_table(int(w.positions.max()) + 1, w.D, w.theta).to(dev)
-
-    stream = torch.cuda.current_stream(dev)
-    out = torch.empty((w.B, w.H, w.D), dtype=w.out_dtype, device=dev)
-    part = torch.empty((w.B, w.H, w.D), dtype=torch.float32, device=dev)
-    lse = torch.empty((w.B, w.H), dtype=torch.float32, device=dev)
-    pool_snapshot = t["kv_pool"].clone() if w.fused else None  # the fused step appends; restore is not timed
-
-    launches_per_step = 1 if (not split and not w.fused) or w.fused else 2
-    exchange = None
-    if split:
-        from cottus_b200 import parallel
-        if args.exchange == "peer":
-            exchange = parallel.PeerExchange(w.B, w.H, w.D)
-
-    def step():
-        if w.fused:
-            cb.rope_append_decode(t["query"], t["key"], t["value"], t["positions"], t["cos_sin"], t["kv_pool"],
-                                  t["block_table"], num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs, out=out)
-        elif split and exchange is not None:
-            # decode kernel (completion flagged to every rank) + combine kernel reading peers over NVLink
-            parallel.split_kv_decode_peer(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], exchange,
-                                          num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
-                                          num_physical_blocks=wl.num_blocks, out_dtype=w.out_dtype, out=out)
-        elif split:
-            parallel.split_kv_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"],
-                                     num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
-                                     num_physical_blocks=wl.num_blocks, out_dtype=w.out_dtype, part=part, lse=lse)
-        else:
-            cb.paged_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], num_kv_heads=w.Hkv,
-                            head_dim=w.D, block_size=w.bs, out=out, num_physical_blocks=wl.num_blocks)
-
-    kv_bytes_rank = wl.kv_bytes()
-    small = w.kv_bytes() < 2 * L2_BYTES
-    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if small else None
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-
-    sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.3)
-    if small:
-        # L2-resident working set: flush L2 between steps, time every step alone
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
-        for i in range(args.steps):
-            flush.fill_(float(i))
-            evs[i][0].record(stream)
-            step()
-            evs[i][1].record(stream)
-        torch.cuda.synchronize(dev)
-        elapsed_ms = sum(a.elapsed_time(b) for a, b in evs)
-    else:
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for _ in range(args.steps):
-            step()
-        e1.record(stream)
-        torch.cuda.synchronize(dev)
-        elapsed_ms = e0.elapsed_time(e1)
-    clocks = sampler.stop()
-    if world > 1:
-        tt = torch.tensor([elapsed_ms], device=dev)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(tt.item())
-    ms = elapsed_ms / args.steps
-
-    # the dominant kernel alone: one decode launch between each event pair
-    ka = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(50)]
-    for a, b in ka:
-        if small:
-            flush.fill_(1.0)
-        a.record(stream)
-        if w.fused:
-            step()
-        else:
-            cb.paged_decode(t["query"], t["kv_pool"], t["block_table"], t["context_lens"], num_kv_heads=w.Hkv,
-                            head_dim=w.D, block_size=w.bs, out=part if split else out, lse_out=lse if split else None,
-                            num_physical_blocks=wl.num_blocks)
-        b.record(stream)
-    torch.cuda.synchronize(dev)
-    k_ms = float(np.mean([a.elapsed_time(b) for a, b in ka]))
-
-    # end to end through the C ABI with host buffers: every step copies its query, table and lengths
-    # from pinned host memory and reads its output back into pinned host memory (pipelined: the
-    # copies of neighbouring steps overlap each kernel)
-    e2e = None
-    if not args.no_e2e and not split and not w.fused:
-        host_in = [t["query"].cpu().pin_memory(), t["block_table"].cpu().pin_memory(),
-                   t["context_lens"].cpu().pin_memory()]
-        e_ms = pipelined_e2e(lambda i, ins, o: cb.paged_decode(ins[0], t["kv_pool"], ins[1], ins[2],
-                                                               num_kv_heads=w.Hkv, head_dim=w.D, block_size=w.bs,
-                                                               out=o, num_physical_blocks=wl.num_blocks),
-                             host_in, out, args, dev, world)
-        h2d = sum(h.numel() * h.element_size() for h in host_in)
-        d2h = out.numel() * out.element_size()
-        e2e = {"value": world * kv_bytes_rank / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
-               "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "api": "cottus_paged_decode (C ABI via ctypes)",
-               "pipelining": "two buffer sets; uploads and read-backs on two copy streams overlap the kernels"}
-
-    if pool_snapshot is not None:
-        t["kv_pool"].copy_(pool_snapshot)
-
-    cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        try:
-            r, threads, sample = cpu_reference_rate(w, t, target_s=8.0,
-                                                    max_seqs=1 if w.name == "long_ctx_70b" else None)
-            cpu = {"value": r, "unit": "GB/s", "cores": threads, "kind": "reference", "sample": sample}
-        except Exception as ex:  # the baseline is reported, never required
-            cpu = {"value": None, "unit": "GB/s", "cores": 0, "kind": "reference", "sample": f"unavailable: {ex}"}
-
-    if exchange is not None:
-        exchange.close()  # collective: every rank is done with the peer buffers
-    if world > 1:
-        dist.barrier()
-    if rank != 0:
-        if world > 1:
-            dist.destroy_process_group()
-        return
-
-    peak, peak_kind = peaks()
-    total_kv = (w.kv_bytes() if split else kv_bytes_rank * world)
-    value = total_kv / (ms * 1e-3) / 1e9
-    alg = kv_bytes_rank + wl.io_bytes()
-    # launch duration for the roofline: where a step is one launch of the
-    # kernel, the timed region per launch (launches back to back, as a decode
-    # loop issues them); otherwise the kernel timed alone between events
-    kern_ms = ms if launches_per_step == 1 else k_ms
-    achieved = alg / (kern_ms * 1e-3) / 1e9
-    mma = (w.H // w.Hkv) > 1 and w.D in (64, 128) and (w.out_dtype == torch.float16 or split)
-    kname = ("decode_mma_kernel" if mma else "decode_tma_kernel") + (" (RoPE + append fused)" if w.fused else "")
-    traffic = None
-    prof = ROOT / "profiles" / "traffic.json"
-    if prof.exists():
-        traffic = json.loads(prof.read_text()).get(w.name)
-    line = {
-        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong" if split else "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic: seeded N(0,1) KV stored via the reference's truncating fp16 encoder",
-        "config": {"workload": describe(w), "kv": "fp16", "q_out": str(w.q_dtype).replace("torch.", ""),
-                   "per_gpu_batch": wl.B, "kv_bytes_per_step_per_gpu": kv_bytes_rank,
-                   "l2": ("L2 flushed between steps (2x L2 buffer written)" if small else
-                          f"inputs larger than L2 ({kv_bytes_rank / 1e6:.0f} MB KV per GPU vs 126 MB L2), no flush"),
-                   "parallelism": ((f"split-KV over {world} GPUs, " +
-                                    ("LSE partials read from peer memory over NVLink after a completion flag raised "
-                                     "by the decode kernel" if exchange is not None else
-                                     "NCCL all-gather of LSE partials")) if split else
-                                   f"sequence-sharded over {world} GPU(s), no collective")},
-        "tokens_per_s": w.B * (1 if split else world) / (ms * 1e-3),
-        "pct_hbm_peak": value / world / peak * 100 if not split else value / world / peak * 100,
-        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": kname + ((" + peer_combine_kernel" if exchange is not None else " + lse_combine_kernel")
-                                        if split else "") + ": one decode launch per step",
-                     "kernel_ms": kern_ms, "kernel_ms_alone": k_ms, "algorithmic_bytes": alg},
-        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
-    }
-    print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.destroy_process_group()
+    {"qkv_llama3_8b": run_qkv, "oproj_llama3_8b": run_oproj,
+     "attn_block_llama3_8b": run_attn_block}.get(args.config, run_decode)(args, rank, world, local)
 
 
 if __name__ == "__main__":

@@ -133,6 +133,7 @@ def lib() -> C.CDLL:
         ("cottus_o_proj_residual", C.c_int, [P(OProjParams), _vp]),
         ("cottus_peer_exchange_create", C.c_int, [_i32, _i32, _i32, _i32, _i32, P(_vp), _vp]),
         ("cottus_peer_exchange_open", C.c_int, [_vp, _vp]),
+        ("cottus_peer_exchange_set_wait_cycles", C.c_int, [_vp, _i64]),
         ("cottus_peer_exchange_destroy", None, [_vp]),
         ("cottus_split_decode_workspace_size", _sz, [P(PagedDecodeParams)]),
         ("cottus_split_decode", C.c_int, [P(PagedDecodeParams), _vp, _vp]),

@@ -60,9 +60,14 @@ def split_kv_decode(query, kv_pool, block_table, context_lens, *, num_kv_heads, 
 class PeerExchange:
     """Exchange buffers of a split-context decode, one per rank, mapped by
     every other rank through CUDA IPC (cottus_peer_exchange_*).  Collective
-    at construction (handles all-gathered over `group`)."""
+    at construction (handles all-gathered over `group`).  `wait_cycles`
+    sets the combine's wait limit in GPU clock cycles (default about 1 s).
+    `absent` lists ranks that take no part (their handles are replaced by
+    all-zero ones): every combine then waits out its limit and reports
+    COTTUS_STATUS_TIMEOUT, which is how failure handling is exercised."""
 
-    def __init__(self, batch: int, num_heads: int, head_dim: int, group=None):
+    def __init__(self, batch: int, num_heads: int, head_dim: int, group=None, wait_cycles: int | None = None,
+                 absent=()):
         world, rank = dist.get_world_size(group), dist.get_rank(group)
         handle = (C.c_uint8 * 64)()
         h = C.c_void_p()
@@ -73,14 +78,44 @@ class PeerExchange:
         every = torch.empty(world * 64, dtype=torch.uint8, device=dev)
         dist.all_gather_into_tensor(every, mine, group=group)
         blob = np.ascontiguousarray(every.cpu().numpy())
-        check(lib().cottus_peer_exchange_open(self._h, blob.ctypes.data))
+        self._open(blob, absent, rank, wait_cycles)
         dist.barrier(group=group)  # every rank mapped every buffer before first use
-        self.group = group
+        self.group, self._collective = group, True
+
+    @classmethod
+    def alone(cls, world: int, rank: int, batch: int, num_heads: int, head_dim: int, wait_cycles: int | None = None):
+        """This process as rank `rank` of `world` ranks of which no other takes
+        part (no process group needed): every combine waits out its limit and
+        reports COTTUS_STATUS_TIMEOUT (world 1: an ordinary one-rank split)."""
+        self = cls.__new__(cls)
+        handle = (C.c_uint8 * 64)()
+        h = C.c_void_p()
+        check(lib().cottus_peer_exchange_create(world, rank, batch, num_heads, head_dim, C.byref(h), handle))
+        self._h = h
+        self.group, self._collective = None, False
+        self._open(np.zeros(world * 64, np.uint8), range(world), rank, wait_cycles)
+        return self
+
+    def _open(self, blob, absent, rank, wait_cycles):
+        blob = blob.copy()
+        for r in absent:
+            if r != rank:
+                blob[r * 64:(r + 1) * 64] = 0
+        try:
+            check(lib().cottus_peer_exchange_open(self._h, blob.ctypes.data))
+            if wait_cycles is not None:
+                check(lib().cottus_peer_exchange_set_wait_cycles(self._h, int(wait_cycles)))
+        except Exception:
+            lib().cottus_peer_exchange_destroy(self._h)
+            self._h = None
+            raise
 
     def close(self):
-        """Collective: every rank stops using the exchange, then frees it."""
+        """Collective (when made with a group): every rank stops using the
+        exchange, then frees it."""
         if self._h:
-            dist.barrier(group=self.group)
+            if self._collective:
+                dist.barrier(group=self.group)
             lib().cottus_peer_exchange_destroy(self._h)
             self._h = None
 

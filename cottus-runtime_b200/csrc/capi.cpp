@@ -170,6 +170,17 @@ size_t cottus_paged_decode_workspace_size(const cottus_paged_decode_params* p) {
 }
 
 int cottus_paged_decode(const cottus_paged_decode_params* p, cottus_stream_t stream) {
+    const int rc = cb200::validate_decode_params(p);
+    if (rc) return rc;
+    return run_decode(desc_from(p), reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"
+
+namespace cb200 {
+// Argument checks of cottus_paged_decode, shared with the entry points that
+// wrap it (they run before anything is sized, allocated or queued).
+int validate_decode_params(const cottus_paged_decode_params* p) {
     if (!p) return fail(COTTUS_ERR_INVALID_ARGUMENT, "params must not be NULL");
     int rc = check_common(p->batch, p->layer, p->num_heads, p->num_kv_heads, p->head_dim, p->block_size,
                           p->num_layers, p->max_blocks_per_seq, p->num_physical_blocks);
@@ -177,23 +188,16 @@ int cottus_paged_decode(const cottus_paged_decode_params* p, cottus_stream_t str
     if (!valid_dtype(p->q_dtype) || !valid_dtype(p->out_dtype)) return fail(COTTUS_ERR_INVALID_ARGUMENT, "unknown dtype");
     if (p->batch > 0 && (!p->out || !p->query || !p->kv_pool || !p->block_table || !p->context_lens))
         return fail(COTTUS_ERR_INVALID_ARGUMENT, "NULL pointer argument");
-    return run_decode(desc_from(p), reinterpret_cast<cudaStream_t>(stream));
+    return COTTUS_OK;
 }
 
-}  // extern "C"
-
-namespace cb200 {
 // cottus_paged_decode whose completion is signalled to the ranks of a split
 // context (peer_exchange.cu): by the fast-path kernel itself, or by a
 // signal kernel after the generic one.
 int paged_decode_signalled(const cottus_paged_decode_params* p, const PeerSignal& sig, cudaStream_t st) {
-    if (!p) return fail(COTTUS_ERR_INVALID_ARGUMENT, "params must not be NULL");
-    int rc = check_common(p->batch, p->layer, p->num_heads, p->num_kv_heads, p->head_dim, p->block_size,
-                          p->num_layers, p->max_blocks_per_seq, p->num_physical_blocks);
+    int rc = validate_decode_params(p);
     if (rc) return rc;
-    if (!valid_dtype(p->q_dtype) || !valid_dtype(p->out_dtype)) return fail(COTTUS_ERR_INVALID_ARGUMENT, "unknown dtype");
-    if (p->batch <= 0 || !p->out || !p->query || !p->kv_pool || !p->block_table || !p->context_lens)
-        return fail(COTTUS_ERR_INVALID_ARGUMENT, "NULL pointer argument or empty batch");
+    if (p->batch <= 0) return fail(COTTUS_ERR_INVALID_ARGUMENT, "empty batch");
     DecodeDesc d = desc_from(p);
     if (tma_supported(d)) {
         d.signal = sig;

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "cottus_b200.h"
 
 namespace cb200 {
@@ -206,5 +208,19 @@ __device__ __forceinline__ void report(uint32_t* status, uint32_t bits) {
 }
 
 __device__ __forceinline__ int32_t div_up(int32_t a, int32_t b) { return (a + b - 1) / b; }
+
+// Plain launch whose return value is this launch's own error (a sticky
+// error left by an earlier, unrelated launch is not picked up and reported
+// as this one's, as cudaGetLastError after <<<>>> would).
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 }  // namespace cb200

@@ -20,6 +20,7 @@
 #include <utility>
 #include <vector>
 
+#include "common.cuh"
 #include "cottus/block_allocator.h"
 #include "cottus_b200.h"
 #include "internal.h"
@@ -208,9 +209,10 @@ int cottus_decode_batch_begin_step(cottus_decode_batch* b, cottus_stream_t strea
                 u.val[u.n] = send[i].second;
                 ++u.n;
             }
-            cb200::table_update_kernel<<<1, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-                u, b->d.device_block_table, b->table_elems(), b->d.device_positions, b->d.device_context_lens);
-            const cudaError_t e = cudaGetLastError();
+            const cudaError_t e = cb200::launch_kernel(cb200::table_update_kernel, dim3(1), dim3(256), 0,
+                                                       reinterpret_cast<cudaStream_t>(stream), u,
+                                                       b->d.device_block_table, b->table_elems(),
+                                                       b->d.device_positions, b->d.device_context_lens);
             if (e != cudaSuccess) return fail(COTTUS_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(e));
         }
     }

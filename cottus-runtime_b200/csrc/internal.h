@@ -99,6 +99,10 @@ cudaError_t launch_gather(uint16_t* k_out, uint16_t* v_out, const uint16_t* kv, 
                           int32_t num_kv_heads, int32_t head_dim, int32_t block_size, int32_t num_layers,
                           int32_t layer, int32_t max_blocks, uint32_t* status, cudaStream_t st);
 
+// Argument checks of cottus_paged_decode (capi.cpp); COTTUS_OK or the
+// error code, with the message set.
+int validate_decode_params(const cottus_paged_decode_params* p);
+
 // Split-context decode (peer_exchange.cu): the decode whose completion is
 // signalled to every rank, and the stand-alone signal used after the
 // generic kernel.

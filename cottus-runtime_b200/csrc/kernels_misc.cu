@@ -178,9 +178,8 @@ cudaError_t launch_decode_generic(const DecodeDesc& d, cudaStream_t st) {
     dim3 grid(d.num_heads, d.batch);
     // In rope mode the query is rotated in fp32 inside the kernel (the
     // append kernel launched before has already written k/v and q_out).
-    if (d.rope) decode_generic_kernel<true><<<grid, kGenThreads, smem, st>>>(a);
-    else decode_generic_kernel<false><<<grid, kGenThreads, smem, st>>>(a);
-    return cudaGetLastError();
+    if (d.rope) return launch_kernel(decode_generic_kernel<true>, grid, dim3(kGenThreads), smem, st, a);
+    return launch_kernel(decode_generic_kernel<false>, grid, dim3(kGenThreads), smem, st, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -283,8 +282,7 @@ cudaError_t launch_rope_append(const DecodeDesc& d, cudaStream_t st) {
     a.maxb = d.max_blocks;
     a.max_pos = d.max_position;
     a.f16 = d.q_f16;
-    rope_append_kernel<<<d.batch, 256, 0, st>>>(a);
-    return cudaGetLastError();
+    return launch_kernel(rope_append_kernel, dim3(d.batch), dim3(256), 0, st, a);
 }
 
 // ---------------------------------------------------------------------------
@@ -316,8 +314,8 @@ cudaError_t launch_rope(float* out, const float* in, const int32_t* positions, i
     const long long total = (long long)num_tokens * H * (D / 2);
     if (total == 0) return cudaSuccess;
     const int blocks = (int)((total + 255) / 256 < 65535 ? (total + 255) / 256 : 65535);
-    rope_kernel<<<blocks, 256, 0, st>>>(out, in, positions, num_tokens, H, D, cos_sin, max_pos);
-    return cudaGetLastError();
+    return launch_kernel(rope_kernel, dim3(blocks), dim3(256), 0, st, out, in, positions, num_tokens, H, D, cos_sin,
+                         max_pos);
 }
 
 // (cos, sin) pairs for one position passed by value (<= 128 pairs).
@@ -342,8 +340,7 @@ cudaError_t launch_rope_single(float* out, const float* in, const float* host_co
     for (int i = 0; i < D && i < 256; ++i) cs.v[i] = host_cos_sin[i];
     const int total = H * (D / 2);
     if (total == 0) return cudaSuccess;
-    rope_single_kernel<<<(total + 255) / 256, 256, 0, st>>>(out, in, cs, H, D);
-    return cudaGetLastError();
+    return launch_kernel(rope_single_kernel, dim3((total + 255) / 256), dim3(256), 0, st, out, in, cs, H, D);
 }
 
 // ---------------------------------------------------------------------------
@@ -378,9 +375,8 @@ cudaError_t launch_lse_combine(void* out, int out_f16, float* lse_out, const flo
     const long long heads = (long long)B * H;
     if (heads == 0) return cudaSuccess;
     const long long threads = heads * 32;
-    lse_combine_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, st>>>(out, out_f16, lse_out, part_out, part_lse, P,
-                                                                        heads, D);
-    return cudaGetLastError();
+    return launch_kernel(lse_combine_kernel, dim3((unsigned)((threads + 255) / 256)), dim3(256), 0, st, out, out_f16,
+                         lse_out, part_out, part_lse, P, heads, D);
 }
 
 // ---------------------------------------------------------------------------
@@ -432,9 +428,8 @@ cudaError_t launch_gather(uint16_t* k_out, uint16_t* v_out, const uint16_t* kv, 
     const int pages = (max_ctx + bs - 1) / bs;
     if (pages == 0 || B == 0) return cudaSuccess;
     dim3 grid(pages, B);
-    gather_kernel<<<grid, 256, 0, st>>>(k_out, v_out, kv, bt, ctx, num_blocks, max_ctx, Hkv, D, bs, L, layer, maxb,
-                                        status);
-    return cudaGetLastError();
+    return launch_kernel(gather_kernel, grid, dim3(256), 0, st, k_out, v_out, kv, bt, ctx, num_blocks, max_ctx, Hkv, D,
+                         bs, L, layer, maxb, status);
 }
 
 }  // namespace cb200

@@ -18,7 +18,10 @@
 // previous call's contents; the arrival counters that must start at zero
 // are cleared (cudaMemsetAsync, no allocation) at every call.  Calls whose
 // executions overlap on the GPU (different streams, no ordering between
-// them) race on the array.
+// them) race on the array.  The looked-up address is kept with the id of
+// the context it belongs to; after a device reset (a new primary context)
+// the next call looks it up again.
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -39,32 +42,65 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
+struct ScratchAddress {
+    unsigned long long ctx = 0;  // id of the context the address belongs to (0: none yet)
+    void* ptr = nullptr;
+};
+ScratchAddress g_scratch[kMaxDevices];
 
-// Device address of the scratch array on the current device (set up once per
-// device with that device current).
+// Unique id of the calling thread's current context, 0 when there is none
+// or the driver does not report it.
+unsigned long long current_context_id() {
+    static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+    static PFN_cuCtxGetId_v12000 get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &p, 4000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(p);
+    });
+    if (!get_current || !get_id) return 0;
+    CUcontext c = nullptr;
+    if (get_current(&c) != CUDA_SUCCESS || !c) return 0;
+    unsigned long long id = 0;
+    return get_id(c, &id) == CUDA_SUCCESS ? id : 0;
+}
+
+// Device address of the scratch array on the current device (looked up with
+// that device current, once per device and context).
 int scratch_address(void** out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cb200::set_error(COTTUS_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(e));
     if (dev < 0 || dev >= kMaxDevices) return cb200::set_error(COTTUS_ERR_UNSUPPORTED, "device index out of range");
     std::lock_guard<std::mutex> lock(g_mu);
-    if (!g_scratch_ptr[dev]) {
+    ScratchAddress& a = g_scratch[dev];
+    const unsigned long long ctx = current_context_id();
+    if (!a.ptr || ctx == 0 || ctx != a.ctx) {
         void* p = nullptr;
         e = cudaGetSymbolAddress(&p, g_static_scratch);
         if (e != cudaSuccess || !p)
             return cb200::set_error(COTTUS_ERR_CUDA, std::string("CUDA error: cudaGetSymbolAddress of the static "
                                                                  "scratch failed: ") + cudaGetErrorString(e));
-        g_scratch_ptr[dev] = p;
+        a.ptr = p;
+        a.ctx = current_context_id();  // the lookup made the device's primary context current if none was
     }
-    *out = g_scratch_ptr[dev];
+    *out = a.ptr;
     return COTTUS_OK;
 }
 
 }  // namespace
 
 extern "C" int cottus_paged_decode_static_scratch(const cottus_paged_decode_params* p, cottus_stream_t stream) {
-    if (!p) return cb200::set_error(COTTUS_ERR_INVALID_ARGUMENT, "params must not be NULL");
+    // the arguments are checked before anything is sized or queued
+    const int bad = cb200::validate_decode_params(p);
+    if (bad) return bad;
     const size_t need = cottus_paged_decode_workspace_size(p);
     if (need > kStaticScratchBytes)
         return cb200::set_error(COTTUS_ERR_WORKSPACE,

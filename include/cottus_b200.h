@@ -114,8 +114,10 @@ int cottus_paged_decode(const cottus_paged_decode_params *p, cottus_stream_t str
  * library keeps until the process exits.  p->workspace and
  * p->workspace_bytes are ignored.  Calls needing more scratch than 32 MiB
  * (see cottus_paged_decode_workspace_size) fail with COTTUS_ERR_WORKSPACE.
- * The first call on a device looks up the array's device address; make that
- * first call before any stream capture.  All calls on a device share the
+ * The first call on a device (and the first after a device reset) looks up
+ * the array's device address; make that first call before any stream
+ * capture.  Arguments are checked as cottus_paged_decode checks them before
+ * anything is queued.  All calls on a device share the
  * array: calls whose executions overlap on the GPU race and must be ordered
  * by the caller.  Nothing is allocated or freed. */
 int cottus_paged_decode_static_scratch(const cottus_paged_decode_params *p, cottus_stream_t stream);
@@ -378,17 +380,33 @@ int cottus_decode_batch_sequence(const cottus_decode_batch *b, int64_t seq_id, i
  * receives the merged output [batch][num_heads][head_dim] and p->lse_out
  * (optional) the merged natural-log LSE.  One decode kernel (partials into
  * this rank's exchange buffer, completion flagged to every rank by its last
- * CTA) and one combine kernel (bounded wait for every rank's flag, then
- * peer loads over NVLink and the merge of cottus_lse_combine).  A rank that
- * does not take part makes the others' combine give up after about a
- * second with COTTUS_STATUS_TIMEOUT in p->status.  At most 8 ranks.
+ * CTA) and one combine kernel (bounded wait until every rank has flagged
+ * this step or a later one, then peer loads over NVLink and the merge of
+ * cottus_lse_combine).  At most 8 ranks.
+ *
+ * Failure detection: a rank that does not take part in a step makes the
+ * others' combine give up after the wait limit (default 2e9 GPU clock
+ * cycles, about a second; cottus_peer_exchange_set_wait_cycles) with
+ * COTTUS_STATUS_TIMEOUT in p->status and the output untouched.  A timeout
+ * marks the exchange broken on every rank: each later combine of any rank
+ * reports COTTUS_STATUS_TIMEOUT at once and writes nothing.  To recover,
+ * every rank synchronises its stream, the ranks agree (host side) that all
+ * of them are done with the exchange, destroy it and create a new one.
  * ---------------------------------------------------------------------- */
 #define COTTUS_IPC_HANDLE_BYTES 64
 typedef struct cottus_peer_exchange cottus_peer_exchange;
 int cottus_peer_exchange_create(int32_t world, int32_t rank, int32_t batch, int32_t num_heads, int32_t head_dim,
                                 cottus_peer_exchange **out, void *ipc_handle /* COTTUS_IPC_HANDLE_BYTES, out */);
-/* handles: world x COTTUS_IPC_HANDLE_BYTES, in rank order (this rank's own is skipped) */
+/* handles: world x COTTUS_IPC_HANDLE_BYTES, in rank order (this rank's own is
+ * skipped).  A handle of all zero bytes stands for a rank that takes no part
+ * (a process that never joined): it gets a stand-in buffer on this GPU whose
+ * flag nothing raises, so every combine of this exchange waits out its limit
+ * and reports COTTUS_STATUS_TIMEOUT.  This lets failure handling be
+ * exercised on one GPU. */
 int cottus_peer_exchange_open(cottus_peer_exchange *ex, const void *handles);
+/* Wait limit of the combine kernel in GPU clock cycles, in [1e3, 1e12]
+ * (default 2e9); applies to the calls made after it. */
+int cottus_peer_exchange_set_wait_cycles(cottus_peer_exchange *ex, int64_t cycles);
 /* call on every rank only after all ranks stopped using the exchange */
 void cottus_peer_exchange_destroy(cottus_peer_exchange *ex);
 /* p->workspace must hold cottus_split_decode_workspace_size(p) bytes (the

@@ -32,3 +32,11 @@ def test_reference_arm_json(config):
     assert d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": d["unit"], "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     assert "workload" in d["config"]
+    if config == "tinyllama_f32":
+        # the reference arm describes the workload with the same config object as the GPU arm
+        sys.path.insert(0, str(ROOT))
+        import argparse
+
+        import bench
+        args = argparse.Namespace(config=config, batch=None, exchange="peer")
+        assert d["config"] == bench.decode_config(args, 1)[1]

@@ -61,6 +61,12 @@ def test_invalid_arguments_rejected_without_gpu():
     assert L.cottus_paged_decode(C.byref(p), None) == _lib.COTTUS_ERR_INVALID_ARGUMENT
     assert L.cottus_paged_decode(None, None) == _lib.COTTUS_ERR_INVALID_ARGUMENT
     assert L.cottus_status_string(-5) == b"workspace"
+    # the allocation-free variant checks its arguments the same way, before sizing or queueing anything
+    for field, val in [("batch", -1), ("layer", 1), ("out_dtype", 9)]:
+        q = _lib.PagedDecodeParams.from_buffer_copy(p)
+        setattr(q, field, val)
+        assert L.cottus_paged_decode_static_scratch(C.byref(q), None) == _lib.COTTUS_ERR_INVALID_ARGUMENT
+    assert L.cottus_paged_decode_static_scratch(None, None) == _lib.COTTUS_ERR_INVALID_ARGUMENT
 
 
 def test_projection_arguments_rejected_without_gpu():

@@ -182,4 +182,3 @@ def test_lse_combine_empty_shard():
     w = torch.softmax(lse, dim=0)
     ref = (w.unsqueeze(-1) * parts.nan_to_num()).sum(0)
     assert max_abs(out, ref) < 1e-5
-    _ = TOL_F16
