@@ -183,6 +183,11 @@ __device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int c
                  "r"(c0), "r"(c1), "r"(c2)
                  : "memory");
 }
+// L1 prefetch of the line holding a global address (a hint: nothing is
+// written, so no later instruction waits on it).
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(p)));
+}
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -208,6 +213,69 @@ __device__ __forceinline__ void report(uint32_t* status, uint32_t bits) {
 }
 
 __device__ __forceinline__ int32_t div_up(int32_t a, int32_t b) { return (a + b - 1) / b; }
+
+// Split-KV merge of one (sequence, head) by one warp: P <= kMergeParts parts,
+// part p with natural-log LSE lse[p][hw] and normalised output row
+// row[p][hw * D .. + D).  lse = log(sum_p exp(lse_p)), out = sum_p
+// exp(lse_p - lse) * row_p, parts in increasing order (the same bits
+// whichever kernel calls it).  All parts' loads are issued together (one
+// round trip even when the parts live in other GPUs' memory); a lane covers
+// 4 consecutive dims.
+constexpr int kMergeParts = 8;
+__device__ __forceinline__ void merge_head_parts(const float* const (&lse)[kMergeParts],
+                                                 const float* const (&row)[kMergeParts], int P, long long hw, int D,
+                                                 int lane, void* out, int out_f16, float* lse_out) {
+    float lp[kMergeParts];
+#pragma unroll
+    for (int p = 0; p < kMergeParts; ++p) lp[p] = p < P ? __ldcg(lse[p] + hw) : -INFINITY;
+    float M = -INFINITY;
+#pragma unroll
+    for (int p = 0; p < kMergeParts; ++p) M = fmaxf(M, lp[p]);
+    float S = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+        for (int p = 0; p < kMergeParts; ++p)
+            if (p < P) S += expf(lp[p] - M);
+    }
+    const float L = M == -INFINITY ? -INFINITY : M + logf(S);
+    float wt[kMergeParts];
+#pragma unroll
+    for (int p = 0; p < kMergeParts; ++p) wt[p] = (p < P && lp[p] != -INFINITY) ? expf(lp[p] - L) : 0.f;
+    for (int d = lane * 4; d < D; d += 128) {
+        float4 x[kMergeParts];
+        const int n = D - d < 4 ? D - d : 4;
+#pragma unroll
+        for (int p = 0; p < kMergeParts; ++p) {
+            x[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (p < P && lp[p] != -INFINITY) {
+                const float* src = row[p] + hw * D + d;
+                if (n == 4 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                    x[p] = __ldcg(reinterpret_cast<const float4*>(src));
+                } else {
+                    x[p].x = __ldcg(src);
+                    if (n > 1) x[p].y = __ldcg(src + 1);
+                    if (n > 2) x[p].z = __ldcg(src + 2);
+                    if (n > 3) x[p].w = __ldcg(src + 3);
+                }
+            }
+        }
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int p = 0; p < kMergeParts; ++p) {
+            if (p < P && lp[p] != -INFINITY) {
+                acc[0] += wt[p] * x[p].x;
+                acc[1] += wt[p] * x[p].y;
+                acc[2] += wt[p] * x[p].z;
+                acc[3] += wt[p] * x[p].w;
+            }
+        }
+        for (int e = 0; e < n; ++e) {
+            if (out_f16) reinterpret_cast<__half*>(out)[hw * D + d + e] = __float2half_rn(acc[e]);
+            else reinterpret_cast<float*>(out)[hw * D + d + e] = acc[e];
+        }
+    }
+    if (lse_out && lane == 0) lse_out[hw] = L;
+}
 
 // Plain launch whose return value is this launch's own error (a sticky
 // error left by an earlier, unrelated launch is not picked up and reported

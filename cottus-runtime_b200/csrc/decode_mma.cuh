@@ -1,9 +1,22 @@
 // Paged decode attention with the QK and PV tile products on the tensor
-// cores (warp-level mma.sync m16n8k16, fp16 inputs, fp32 accumulation).
+// cores (warp-level mma.sync m16n8k16, fp16 inputs, fp32 accumulation),
+// one CTA per stream-K worker.
 //
-// Same stream-K schedule, per-warp TMA ring, merge and epilogue contract as
-// decode_tma_kernel; only the math per page differs:
+// Schedule.  Units are (sequence, kv head, page) in sequence-major order,
+// as in decode_tma_kernel, but the worker is a whole CTA: CTA c owns one
+// contiguous chunk of ceil(units / CTAs) units.  A chunk is a list of
+// segments, its intersection with each (sequence, kv head) pair.  The 4
+// warps split every segment's pages (unit k of the chunk goes to warp
+// k mod 4), each warp with its own TMA ring and its own online-softmax
+// state; at the end of a segment the warps' (m, l, o) states are merged in
+// shared memory and the whole CTA writes the pair's output (or, for a pair
+// cut by chunk boundaries, one partial per chunk; the last CTA to finish
+// such a pair merges the partials).  Against one warp per chunk, a pair is
+// cut into 4x fewer parts, so the merges that end a launch are 4x shorter
+// and their arrival counters see little contention, and a warp's block-table
+// entries for the first pages are loaded in parallel, not one after another.
 //
+// Math per page and warp:
 //   S^T[16 tokens x 8 cols] = K[16 x D] . Q^T[D x 8]      (D/16 MMAs)
 //       A = the page's K rows (ldmatrix from a 128B-swizzled TMA tile),
 //       B = the GQA group's query rows (columns >= G are zero), kept in
@@ -59,30 +72,223 @@ __device__ __forceinline__ uint32_t swz(int region, int row, int chunk) {
     return (uint32_t)(region * (32 * 128) + row * 128 + ((chunk ^ (row & 7)) << 4));
 }
 
-template <int D>
+template <int D, int G>
 struct MmaCfg {
     static constexpr int KSTEPS = D / 16;   // QK k-steps = PV dim tiles
     static constexpr int REGIONS = D / 64;  // 128-byte column regions per slot
     static constexpr int SLOT_BYTES = 2 * kBS * D * 2;
+    static constexpr int OST = D + 4;       // head stride of the merge area in floats (padded: no bank conflicts)
+    static constexpr int MERGE_FLOATS = kNW * G * OST + kNW * G * 2;
 };
 
-template <int RING, int D>
+template <int RING, int D, int G>
 constexpr size_t mma_smem_bytes() {
-    return (size_t)kNW * RING * MmaCfg<D>::SLOT_BYTES + (size_t)kNW * RING * 8 + (size_t)kNW * RING * 4 + 1024;
+    using C = MmaCfg<D, G>;
+    return (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 8 + (size_t)kNW * RING * 4 +
+           (size_t)C::MERGE_FLOATS * 4 + 1024 + 16;
 }
 
-// CTAs per SM the register budget is fitted to: two.  Three (168
-// registers) keep more pages in flight, but the launch then has 1.5x the
-// workers, so more (sequence, kv head) pairs are cut between workers and
-// merged at the end: measured on the Llama-3-8B shape (batch 64, context
-// 2048), 94.8 us per step with three against 90.5 us with two.
-constexpr int kMmaMinCtas = 2;
+// CTAs per SM the register budget is fitted to (8 or 12 warps per SM).
+#ifndef CB200_MMA_MIN_CTAS_D64
+#define CB200_MMA_MIN_CTAS_D64 2
+#endif
+#ifndef CB200_MMA_MIN_CTAS_D128
+#define CB200_MMA_MIN_CTAS_D128 2
+#endif
+template <int D>
+constexpr int mma_min_ctas() { return D == 64 ? CB200_MMA_MIN_CTAS_D64 : CB200_MMA_MIN_CTAS_D128; }
+
+// Virtual units after each pair's pages in the partition into chunks: a
+// pair's fixed cost (staging and rotating its query, the warps' merge at
+// its end, the arrival of a cut pair) counted in units, so that a chunk
+// full of short pairs gets fewer pages.  Cursors skip them.
+#ifndef CB200_PAIR_PAD_D64
+#define CB200_PAIR_PAD_D64 24
+#endif
+#ifndef CB200_PAIR_PAD_D128
+#define CB200_PAIR_PAD_D128 8
+#endif
+template <int D>
+constexpr int pair_pad() { return D == 64 ? CB200_PAIR_PAD_D64 : CB200_PAIR_PAD_D128; }
+// Fewest units in a CTA's chunk (4 per warp).
+constexpr long long kMinChunkCta = 4 * kNW;
+
+// One segment of a chunk [u0, u1): the chunk's real units inside one
+// (sequence, kv head) pair.  c is at the segment's first page, r0 counts
+// the chunk's real units before it, len is its number of pages (0: the
+// chunk has no further segment).
+struct Segment {
+    Cursor c;
+    int r0, len;
+};
+
+// Real pages of the pair at c (from page c.p) that lie before unit u1.
+__device__ __forceinline__ int pages_before(const Cursor& c, const TmaArgs& a, long long u1) {
+    if (c.b >= a.B || c.ps + c.p >= u1) return 0;
+    return (int)min((long long)c.np, u1 - c.ps) - c.p;
+}
+
+template <bool ROPE, int PAD>
+__device__ __forceinline__ void next_segment(Segment& s, const TmaArgs& a, long long u1) {
+    s.r0 += s.len;
+    s.c.p = s.c.np - 1;
+    cursor_next<ROPE>(s.c, a, PAD);  // page 0 of the next pair
+    s.len = pages_before(s.c, a, u1);
+}
+
+// Moves c forward by n real units (n small).
+template <bool ROPE, int PAD>
+__device__ __forceinline__ void cursor_advance(Cursor& c, const TmaArgs& a, int n) {
+    if (c.p + n < c.np) {  // within the pair: the common case
+        c.p += n;
+        return;
+    }
+    for (int i = 0; i < n; ++i) cursor_next<ROPE>(c, a, PAD);
+}
+
+// The new token of a pair (fused step), lane < D/8 of the warp that owns the
+// pair's last page: rotates k, encodes k and v by truncation, writes them to
+// slot t_new of the page in the pool and in the page's shared-memory tile
+// `sl` (so the token attends to itself).  Out of line: it runs once per pair,
+// and keeping it out of the page loop keeps that loop's code compact.
+template <int D>
+__device__ __noinline__ void append_new_token(uint8_t* sl, uint16_t* kv, const void* k_new, const void* v_new,
+                                            const float* cos_sin, int qkv_f16, long long blk, int L, int layer,
+                                            int Hkv, int b, int h, int ctx, int lane) {
+    const int t_new = (ctx - 1) % kBS;
+    const long long src = ((long long)b * Hkv + h) * D + lane * 8;
+    float kx[8], vx[8];
+    if (qkv_f16) {
+        load8(reinterpret_cast<const __half*>(k_new) + src, kx);
+        load8(reinterpret_cast<const __half*>(v_new) + src, vx);
+    } else {
+        load8(reinterpret_cast<const float*>(k_new) + src, kx);
+        load8(reinterpret_cast<const float*>(v_new) + src, vx);
+    }
+    const float4* cs = reinterpret_cast<const float4*>(cos_sin + ((long long)(ctx - 1) * (D / 2) + lane * 4) * 2);
+#pragma unroll
+    for (int pr = 0; pr < 2; ++pr) {
+        const float4 c4 = __ldg(cs + pr);
+        rope_pair(kx[4 * pr], kx[4 * pr + 1], c4.x, c4.y, kx[4 * pr], kx[4 * pr + 1]);
+        rope_pair(kx[4 * pr + 2], kx[4 * pr + 3], c4.z, c4.w, kx[4 * pr + 2], kx[4 * pr + 3]);
+    }
+    uint32_t kw[4], vw[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        kw[j] = (uint32_t)f32_to_f16_trunc(kx[2 * j]) | ((uint32_t)f32_to_f16_trunc(kx[2 * j + 1]) << 16);
+        vw[j] = (uint32_t)f32_to_f16_trunc(vx[2 * j]) | ((uint32_t)f32_to_f16_trunc(vx[2 * j + 1]) << 16);
+    }
+    const uint4 k4 = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+    const uint4 v4 = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+    *reinterpret_cast<uint4*>(sl + swz(lane / 8, t_new, lane % 8)) = k4;
+    *reinterpret_cast<uint4*>(sl + swz(lane / 8, kBS + t_new, lane % 8)) = v4;
+    const long long row0 = (blk * L + layer) * (2 * kBS);
+    *reinterpret_cast<uint4*>(kv + ((row0 + t_new) * Hkv + h) * D + lane * 8) = k4;
+    *reinterpret_cast<uint4*>(kv + ((row0 + kBS + t_new) * Hkv + h) * D + lane * 8) = v4;
+}
+
+// Arrival of a cut pair (every thread of the CTA has stored its part of the
+// pair's partial) on the pair's counter, tagged with the launch epoch so that
+// a count left by an aborted launch, or bytes of another layout that used the
+// same workspace, read as zero (a completed pair leaves its counter at zero,
+// which a CUDA-graph replay with the same tag needs); the CTA that completes
+// the pair merges all its parts.  Chunk c owns units [c*chunk, (c+1)*chunk),
+// so the parts of a pair whose pages are units [ps, ps + np) belong to chunks
+// ps/chunk .. (ps+np-1)/chunk; a chunk's part is in slot 2c when the pair
+// starts at or before the chunk, else in slot 2c+1.  Called by every thread of
+// the CTA; out of line (see append_new_token).
+// The launch's fields that the arrival and merge read (passed by value: a
+// reference to the kernel's argument block would copy it to local memory).
+struct MergeArgs {
+    unsigned long long* counters;
+    const float* ws_o;
+    const float* ws_ml;
+    void* out;
+    float* lse;
+    int H, Hkv, out_f16;
+    unsigned epoch;
+};
+
+template <int D, int G>
+__device__ __noinline__ void arrive_cut_pair(const MergeArgs a, long long chunk, int pb, int ph, int pnp, long long pps,
+                                           unsigned long long hint, int* s_last) {
+    const long long w0 = pps / chunk, w1 = (pps + pnp - 1) / chunk;
+    const int nparts = (int)(w1 - w0 + 1);
+    fence_acq_rel_gpu();  // this thread's partial stores are visible device-wide before the arrival
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long* ctr = a.counters + 1 + (long long)pb * a.Hkv + ph;
+        unsigned long long old = hint;
+        int last = 0;
+        while (true) {  // a failed attempt means another part arrived: at most nparts rounds
+            const unsigned long long nv =
+                (unsigned)(old >> 32) == a.epoch ? old + 1 : (((unsigned long long)a.epoch << 32) | 1ull);
+            const bool fin = (int)(nv & 0xffffffffull) == nparts;
+            const unsigned long long prev = atomicCAS(ctr, old, fin ? 0ull : nv);
+            if (prev == old) {
+                last = fin;
+                break;
+            }
+            old = prev;
+        }
+        *s_last = last;
+    }
+    __syncthreads();
+    if (!*s_last) return;
+    fence_acq_rel_gpu();
+    const long long slot0 = w0 * chunk >= pps ? 2 * w0 : 2 * w0 + 1;  // later parts start inside the pair
+    constexpr int PB = 4;  // parts loaded together
+    constexpr int ITEMS = G * D / 4;
+    for (int it = threadIdx.x; it < ITEMS; it += kNW * 32) {
+        const int g = it / (D / 4), c4 = it % (D / 4);
+        float M = -INFINITY, L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+        for (int j0 = 0; j0 < nparts; j0 += PB) {
+            float2 ml[PB];
+            float4 x[PB];
+#pragma unroll
+            for (int q = 0; q < PB; ++q) {
+                ml[q] = make_float2(-INFINITY, 0.f);
+                x[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (j0 + q < nparts) {
+                    const long long sl = j0 + q == 0 ? slot0 : 2 * (w0 + j0 + q);
+                    ml[q] = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + (sl * G + g) * 2));
+                    x[q] = __ldcg(reinterpret_cast<const float4*>(a.ws_o + (sl * G + g) * D + c4 * 4));
+                }
+            }
+#pragma unroll
+            for (int q = 0; q < PB; ++q) {
+                const float m = ml[q].x;
+                if (m == -INFINITY) continue;  // a part without valid tokens (or past the last part)
+                const float Mn = fmaxf(M, m);
+                const float sa = exp2f(M - Mn), sb = exp2f(m - Mn);
+                M = Mn;
+                L = L * sa + ml[q].y * sb;
+                acc.x = acc.x * sa + x[q].x * sb;
+                acc.y = acc.y * sa + x[q].y * sb;
+                acc.z = acc.z * sa + x[q].z * sb;
+                acc.w = acc.w * sa + x[q].w * sb;
+            }
+        }
+        const float inv = L > 0.f ? 1.f / L : 0.f;
+        const long long head = (long long)pb * a.H + (long long)ph * G + g;
+        if (a.out_f16) {
+            *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(a.out) + head * D + c4 * 4) =
+                make_uint2(pack_h2(acc.x * inv, acc.y * inv), pack_h2(acc.z * inv, acc.w * inv));
+        } else {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + head * D + c4 * 4) =
+                make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        }
+        if (a.lse && c4 == 0) a.lse[head] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+    }
+}
 
 template <int D, int G, int RING, bool ROPE, bool QSPLIT, bool PSPLIT>
-__global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
+__global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D>())
     decode_mma_kernel(const __grid_constant__ CUtensorMap kv_map, const TmaArgs a) {
-    using C = MmaCfg<D>;
-    constexpr int KS = C::KSTEPS, REG = C::REGIONS, LW = D / 8;
+    using C = MmaCfg<D, G>;
+    constexpr int KS = C::KSTEPS, REG = C::REGIONS, LW = D / 8, OST = C::OST, PAD = pair_pad<D>();
     constexpr unsigned FULL = 0xffffffffu;
     static_assert(G <= 8, "group larger than the MMA n dimension");
 
@@ -93,12 +299,17 @@ __global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)kNW * RING * C::SLOT_BYTES) + warp * RING;
     int* slot_blk =
         reinterpret_cast<int*>(smem + (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 8) + warp * RING;
+    float* merge_o = reinterpret_cast<float*>(
+        (reinterpret_cast<uintptr_t>(smem + (size_t)kNW * RING * C::SLOT_BYTES + (size_t)kNW * RING * 12) + 15) &
+        ~uintptr_t(15));                    // [kNW][G][OST]
+    float* merge_ml = merge_o + kNW * G * OST;  // [kNW][G][2]
 
-    __shared__ unsigned cta_done;  // warps of this CTA that finished (split-context signal)
+    __shared__ int s_abort;  // a warp of this CTA gave up on a wait
+    __shared__ int s_last;   // this CTA is the last to finish a cut pair
     if (lane == 0) {
         if (warp == 0) {
             prefetch_tensormap(&kv_map);
-            cta_done = 0;
+            s_abort = 0;
         }
 #pragma unroll
         for (int r = 0; r < RING; ++r) mbar_init(&bars[r], 1);
@@ -106,14 +317,46 @@ __global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
     }
     __syncthreads();
 
-    const long long W = (long long)gridDim.x * kNW;
-    const long long w = (long long)blockIdx.x * kNW + warp;
-    warm_first_pages<ROPE>(a, &kv_map, w, W, lane, REG, 64);
+    const long long W = gridDim.x, cid = blockIdx.x;
+    // The plan is made before the wait for the preceding kernel, from a
+    // snapshot of the lengths that kernel may still be writing, and the warp's
+    // first pages are warmed in L2 from it (TMA prefetch: nothing written;
+    // block ids range-checked, the tensor map bounds the box; L2 is the point
+    // of coherence, so a stale snapshot only warms the wrong lines).  After
+    // the wait the lengths are read again: the plan is kept if they match,
+    // else made again.  Batches above kPlanRegs * 32 sequences plan after the
+    // wait only.
+    const bool small = a.B <= 32 * kPlanRegs;
+    PlanRegs snap;
+    WorkerPlan pl;
+    if (small) {
+        snap = load_plan_regs<ROPE>(a, lane);
+        pl = plan_from_regs<ROPE>(a, snap, cid, W, lane, kMinChunkCta, PAD);
+        if (pl.u0 < pl.u1 && pages_before(pl.cur, a, pl.u1) > 0) {
+            Cursor wc = pl.cur;
+            cursor_advance<ROPE, PAD>(wc, a, warp);
+            for (int i = 0; i < kWarmPages && wc.b < a.B && wc.ps + wc.p < pl.u1; ++i) {
+                if (lane == 0 && wc.p < a.maxb) {
+                    const int blk = a.bt[(long long)wc.b * a.maxb + wc.p];
+                    if (blk >= 0 && (long long)blk < a.num_blocks)
+                        for (int q = 0; q < REG; ++q)
+                            tma_prefetch_l2_3d(&kv_map, q * 64, wc.h, (blk * a.L + a.layer) * (2 * kBS));
+                }
+                cursor_advance<ROPE, PAD>(wc, a, kNW);
+            }
+        }
+    }
     grid_dependency_wait();
     grid_dependents_launch();
-    const WorkerPlan pl = plan_worker<D, ROPE>(a, w, W, lane);
-    const long long U = pl.U, chunk = pl.chunk;
-    const long long NC = (U + chunk - 1) / chunk;
+    if (small) {
+        const PlanRegs now = load_plan_regs<ROPE>(a, lane);
+        if (!same_plan_regs<ROPE>(snap, now)) pl = plan_from_regs<ROPE>(a, now, cid, W, lane, kMinChunkCta, PAD);
+        if (warp == 0) zero_fill_from_regs<D, ROPE>(a, now, cid, lane);
+    } else {
+        pl = plan_worker<D, ROPE>(a, cid, W, lane, kMinChunkCta, warp == 0, PAD);
+    }
+    const long long chunk = pl.chunk, u0 = pl.u0, u1 = pl.u1;
+    const bool has_work = u0 < u1 && pages_before(pl.cur, a, u1) > 0;
 
     // fragment coordinates of this lane
     const int qc = lane & 3;   // column pair: heads 2qc, 2qc+1 of C fragments
@@ -124,14 +367,18 @@ __global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
     uint32_t qb[KS][2];
     uint32_t ql[QSPLIT ? KS : 1][2];
     float o[KS][4];
-    // query of the next segment, loaded a page early: raw fp32 values where
-    // they get split (fp32 or rotated queries), else the fp16 pairs as stored
+    // query of the next segment, loaded a segment early and kept as loaded (so
+    // that nothing waits for the loads before the segment starts): fp32 values,
+    // or fp16 pairs as stored (in qs as bit patterns where they get split,
+    // in qn where they are used as they are); with RoPE also the (cos, sin)
+    // pairs of the two dims pairs this lane rotates per k-step
     float qs[QSPLIT ? KS : 1][4];
     uint32_t qn[QSPLIT ? 1 : KS][2];
+    float2 csn[ROPE ? KS : 1][2];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
 
     // this lane's query elements of pair (b, h): head qr, dims kk*16 + 2qc + {0, 1, 8, 9}
-    auto load_q = [&](int b, int h) {
+    auto load_q = [&](int b, int h, int n) {
         const bool live = qr < G;
         const long long qrow = ((long long)b * a.H + (long long)h * G + (live ? qr : 0)) * D;
 #pragma unroll
@@ -142,168 +389,180 @@ __global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
                 qn[kk][0] = live ? __ldg(qh + d0 / 2) : 0u;
                 qn[kk][1] = live ? __ldg(qh + d1 / 2) : 0u;
             } else {
-                float2 u = make_float2(0.f, 0.f), v = make_float2(0.f, 0.f);
-                if (live) {
-                    if (a.q_f16) {
-                        u = unpack_h2(__ldg(reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow + d0)));
-                        v = unpack_h2(__ldg(reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow + d1)));
-                    } else {
-                        u = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d0));
-                        v = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d1));
-                    }
+                if (!live) {
+                    qs[kk][0] = qs[kk][1] = qs[kk][2] = qs[kk][3] = 0.f;
+                } else if (a.q_f16) {
+                    const unsigned* qh = reinterpret_cast<const unsigned*>(reinterpret_cast<const __half*>(a.q) + qrow);
+                    qs[kk][0] = __uint_as_float(__ldg(qh + d0 / 2));
+                    qs[kk][1] = __uint_as_float(__ldg(qh + d1 / 2));
+                } else {
+                    const float2 u = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d0));
+                    const float2 v = __ldg(reinterpret_cast<const float2*>(reinterpret_cast<const float*>(a.q) + qrow + d1));
+                    qs[kk][0] = u.x; qs[kk][1] = u.y; qs[kk][2] = v.x; qs[kk][3] = v.y;
                 }
-                qs[kk][0] = u.x; qs[kk][1] = u.y; qs[kk][2] = v.x; qs[kk][3] = v.y;
+                if constexpr (ROPE) {
+                    const float* cs = a.cos_sin + (long long)(n - 1) * D;  // row of D/2 (cos, sin) pairs
+                    csn[kk][0] = live ? __ldg(reinterpret_cast<const float2*>(cs + d0)) : make_float2(1.f, 0.f);
+                    csn[kk][1] = live ? __ldg(reinterpret_cast<const float2*>(cs + d1)) : make_float2(1.f, 0.f);
+                }
             }
         }
     };
 
-    // ---- work: static chunk w, then chunks from the queue ------------------
-    long long cid = w < NC ? w : (NC > W ? grab_chunk(a, W, NC, lane) : NC);
-    Cursor cur = pl.cur;
-    bool have_cur = w < NC;  // the plan located chunk w's first unit
-    int kg = 0;              // units consumed by this warp so far (ring slot / phase counter)
-
-    while (cid < NC) {
-        const long long u0 = cid * chunk, u1 = min(u0 + chunk, U);
-        const int nu = (int)(u1 - u0);
-        if (!have_cur) cur = locate_unit<ROPE>(a, u0, lane);
-        have_cur = false;
-
-        // ---- TMA issue (lane 0), block id prefetched one page ahead ----------
-        Cursor ic = cur;
-        int blk_next = lane == 0 ? a.bt[(long long)ic.b * a.maxb + ic.p] : 0;
-        auto issue = [&](int k) {
-            if (lane == 0) {
-                const int slot = (kg + k) % RING;
-                const int blk = blk_next;
-                slot_blk[slot] = blk;
-                if (blk < 0 || (long long)blk >= a.num_blocks) {
-                    mbar_arrive(&bars[slot]);
-                } else {
-                    mbar_arrive_expect_tx(&bars[slot], C::SLOT_BYTES);
-                    const int row0 = (blk * a.L + a.layer) * (2 * kBS);
+    // ---- this warp's units: the chunk's real units warp, warp + 4, ... -------
+    auto valid = [&](const Cursor& c) { return c.b < a.B && c.ps + c.p < u1; };
+    int issued = 0, mine = 0;
+    Cursor ic = pl.cur;  // issue cursor: at this warp's next unit to load
+    bool ic_ok = false;  // ic is inside the chunk
+    int blk_next = 0;    // (lane 0) block id of the unit at ic
+    auto issue_one = [&](bool load_next) {
+        if (lane == 0) {
+            const int slot = issued % RING;
+            const int blk = blk_next;
+            slot_blk[slot] = blk;
+            if (blk < 0 || (long long)blk >= a.num_blocks) {
+                mbar_arrive(&bars[slot]);  // nothing to load; the consumer masks the page
+            } else {
+                mbar_arrive_expect_tx(&bars[slot], C::SLOT_BYTES);
+                const int row0 = (blk * a.L + a.layer) * (2 * kBS);
 #pragma unroll
-                    for (int r = 0; r < REG; ++r)
-                        tma_load_3d(slots + (size_t)slot * C::SLOT_BYTES + r * (32 * 128), &kv_map, &bars[slot], 64 * r,
-                                    ic.h, row0);
-                }
-                cursor_next<ROPE>(ic, a);
-                if (k + 1 < nu) blk_next = a.bt[(long long)ic.b * a.maxb + ic.p];
+                for (int r = 0; r < REG; ++r)
+                    tma_load_3d(slots + (size_t)slot * C::SLOT_BYTES + r * (32 * 128), &kv_map, &bars[slot], 64 * r,
+                                ic.h, row0);
             }
-        };
-        const int prime = nu < RING ? nu : RING;
-        for (int k = 0; k < prime; ++k) issue(k);
-        load_q(cur.b, cur.h);
+        }
+        ++issued;
+        cursor_advance<ROPE, PAD>(ic, a, kNW);
+        ic_ok = valid(ic);
+        if (ic_ok) {
+            if (load_next && lane == 0) {
+                const int32_t* row = a.bt + (long long)ic.b * a.maxb;
+                blk_next = row[ic.p];
+                // the table line 8 own units ahead (own pages are kNW apart), so that
+                // the load above hits L1 when it gets there
+                if (ic.p + 8 * kNW < ic.np) prefetch_l1(row + ic.p + 8 * kNW);
+            }
+        }
+    };
+    // drains this warp's loads still in flight (bounded) before it leaves
+    auto drain = [&]() {
+        for (int j = mine; j < issued; ++j) (void)mbar_wait_bounded(&bars[j % RING], (j / RING) & 1);
+        mine = issued;
+    };
 
-        bool seg_open = false, seg_first = true;
-        int seg_start_p = 0;
-        unsigned long long ctr_hint = 0;  // arrival counter of the open segment's pair, read a page early
-        for (int k = 0; k < nu; ++k) {
-            const int slot = (kg + k) % RING;
-            const int ctx_b = cur.n;
-            if (!seg_open) {
-                // ---- segment start: (rotate,) split and pack the staged query ----
-                seg_open = true;
-                seg_first = (k == 0);
-                seg_start_p = cur.p;
-                ctr_hint = 0;
-                m0 = m1 = -INFINITY;
-                l0 = l1 = 0.f;
-                const bool live = qr < G;
-                const long long qrow = ((long long)cur.b * a.H + (long long)cur.h * G + (live ? qr : 0)) * D;
+    if (has_work) {
+        // prime the ring: the block ids of the first RING own units are loaded by
+        // RING lanes at once, then lane 0 issues the loads back to back
+        cursor_advance<ROPE, PAD>(ic, a, warp);
+        ic_ok = valid(ic);
+        int prime = 0, my_blk = 0;
+        {
+            Cursor pc = ic;
+            bool pc_ok = ic_ok;
+            while (pc_ok && prime < RING) {
+                if (lane == prime) my_blk = a.bt[(long long)pc.b * a.maxb + pc.p];
+                ++prime;
+                cursor_advance<ROPE, PAD>(pc, a, kNW);
+                pc_ok = valid(pc);
+            }
+        }
+        for (int j = 0; j < prime; ++j) {
+            blk_next = __shfl_sync(FULL, my_blk, j);
+            issue_one(false);
+        }
+        if (ic_ok && lane == 0) blk_next = a.bt[(long long)ic.b * a.maxb + ic.p];
+    }
+
+    Segment seg;
+    seg.c = pl.cur;
+    seg.r0 = 0;
+    seg.len = has_work ? pages_before(pl.cur, a, u1) : 0;
+    if (has_work) load_q(seg.c.b, seg.c.h, seg.c.n);
+
+    bool ok = true;  // this warp's waits all completed
+    while (seg.len > 0) {
+        const int ctx_b = seg.c.n;
+        const bool whole = seg.c.p == 0 && seg.len == seg.c.np;
+        // ---- segment start: (rotate,) split and pack the staged query ----------
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.f;
+        {
+            const bool live = qr < G;
+            const long long qrow = ((long long)seg.c.b * a.H + (long long)seg.c.h * G + (live ? qr : 0)) * D;
 #pragma unroll
-                for (int kk = 0; kk < KS; ++kk) {
-                    if constexpr (!QSPLIT) {
-                        qb[kk][0] = qn[kk][0];
-                        qb[kk][1] = qn[kk][1];
-                    } else {
-                        const int d0 = kk * 16 + 2 * qc, d1 = d0 + 8;
-                        float x[4] = {qs[kk][0], qs[kk][1], qs[kk][2], qs[kk][3]};
-                        if (ROPE && live) {
-                            const float* cs = a.cos_sin + (long long)(ctx_b - 1) * D;  // row of D/2 (cos, sin) pairs
-                            const float2 c0 = *reinterpret_cast<const float2*>(cs + d0);
-                            const float2 c1 = *reinterpret_cast<const float2*>(cs + d1);
-                            rope_pair(x[0], x[1], c0.x, c0.y, x[0], x[1]);
-                            rope_pair(x[2], x[3], c1.x, c1.y, x[2], x[3]);
-                            if (a.q_out && cur.p == 0) {
-                                if (a.q_f16) {
-                                    *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d0) = pack_h2(x[0], x[1]);
-                                    *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d1) = pack_h2(x[2], x[3]);
-                                } else {
-                                    *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d0) = make_float2(x[0], x[1]);
-                                    *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d1) = make_float2(x[2], x[3]);
-                                }
+            for (int kk = 0; kk < KS; ++kk) {
+                if constexpr (!QSPLIT) {
+                    qb[kk][0] = qn[kk][0];
+                    qb[kk][1] = qn[kk][1];
+                } else {
+                    const int d0 = kk * 16 + 2 * qc, d1 = d0 + 8;
+                    float x[4] = {qs[kk][0], qs[kk][1], qs[kk][2], qs[kk][3]};
+                    if (a.q_f16) {  // staged as fp16 pairs
+                        const float2 u = unpack_h2(__float_as_uint(qs[kk][0])), v = unpack_h2(__float_as_uint(qs[kk][1]));
+                        x[0] = u.x; x[1] = u.y; x[2] = v.x; x[3] = v.y;
+                    }
+                    if (ROPE && live) {
+                        const float2 c0 = csn[kk][0], c1 = csn[kk][1];
+                        rope_pair(x[0], x[1], c0.x, c0.y, x[0], x[1]);
+                        rope_pair(x[2], x[3], c1.x, c1.y, x[2], x[3]);
+                        if (a.q_out && seg.c.p == 0 && warp == 0) {
+                            if (a.q_f16) {
+                                *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d0) = pack_h2(x[0], x[1]);
+                                *reinterpret_cast<uint32_t*>(reinterpret_cast<__half*>(a.q_out) + qrow + d1) = pack_h2(x[2], x[3]);
+                            } else {
+                                *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d0) = make_float2(x[0], x[1]);
+                                *reinterpret_cast<float2*>(reinterpret_cast<float*>(a.q_out) + qrow + d1) = make_float2(x[2], x[3]);
                             }
                         }
-                        qb[kk][0] = pack_h2(x[0], x[1]);
-                        qb[kk][1] = pack_h2(x[2], x[3]);
-                        if constexpr (QSPLIT) {
-                            const float2 hA = unpack_h2(qb[kk][0]), hB = unpack_h2(qb[kk][1]);
-                            ql[kk][0] = pack_h2(x[0] - hA.x, x[1] - hA.y);
-                            ql[kk][1] = pack_h2(x[2] - hB.x, x[3] - hB.y);
-                        }
                     }
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) o[kk][i] = 0.f;
+                    qb[kk][0] = pack_h2(x[0], x[1]);
+                    qb[kk][1] = pack_h2(x[2], x[3]);
+                    if constexpr (QSPLIT) {
+                        const float2 hA = unpack_h2(qb[kk][0]), hB = unpack_h2(qb[kk][1]);
+                        ql[kk][0] = pack_h2(x[0] - hA.x, x[1] - hA.y);
+                        ql[kk][1] = pack_h2(x[2] - hB.x, x[3] - hB.y);
+                    }
                 }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[kk][i] = 0.f;
             }
-            if (cur.p == cur.np - 1 && k + 1 < nu) {
-                // this page ends the segment: stage the next pair's query now so
-                // the load latency hides behind this page's math
-                Cursor nx = cur;
-                cursor_next<ROPE>(nx, a);
-                load_q(nx.b, nx.h);
-            }
+        }
+        // stage the next segment's query now: its loads overlap this segment's pages
+        unsigned long long ctr_hint = 0;  // the pair's arrival counter, read a segment early
+        {
+            Segment nx = seg;
+            next_segment<ROPE, PAD>(nx, a, u1);
+            if (nx.len > 0) load_q(nx.c.b, nx.c.h, nx.c.n);
+            if (!whole && threadIdx.x == 0)
+                ctr_hint = ld_relaxed_u64(a.counters + 1 + (long long)seg.c.b * a.Hkv + seg.c.h);
+        }
 
-            const bool landed = __all_sync(FULL, mbar_wait_bounded(&bars[slot], ((kg + k) / RING) & 1));
-            if (!landed) {
-                if (lane == 0) report(a.status, COTTUS_STATUS_TIMEOUT);
-                for (int kk = k + 1; kk < k + RING && kk < nu; ++kk)
-                    (void)__all_sync(FULL, mbar_wait_bounded(&bars[(kg + kk) % RING], ((kg + kk) / RING) & 1));
-                return;
+        // ---- this warp's pages of the segment ----------------------------------
+        const int o0 = ((warp - seg.r0) % kNW + kNW) % kNW;
+        for (int off = o0; off < seg.len && ok; off += kNW) {
+            const int p = seg.c.p + off;
+            const int slot = mine % RING;
+            ok = __all_sync(FULL, mbar_wait_bounded(&bars[slot], (mine / RING) & 1));
+            if (!ok) {
+                if (lane == 0) {
+                    report(a.status, COTTUS_STATUS_TIMEOUT);
+                    s_abort = 1;
+                }
+                ++mine;
+                drain();
+                break;
             }
             const int blk = slot_blk[slot];
             const bool blk_ok = blk >= 0 && (long long)blk < a.num_blocks;
             if (!blk_ok && lane == 0) report(a.status, COTTUS_STATUS_BAD_BLOCK_ID);
-            int n_valid = blk_ok ? ctx_b - cur.p * kBS : 0;
+            int n_valid = blk_ok ? ctx_b - p * kBS : 0;
             n_valid = n_valid > kBS ? kBS : n_valid;
             uint8_t* sl = slots + (size_t)slot * C::SLOT_BYTES;
             const uint32_t sl_s = slots_s + (uint32_t)(slot * C::SLOT_BYTES);
 
-            if (ROPE && blk_ok && cur.p == cur.np - 1 && lane < LW) {
-                // the new token: rotate k, encode k and v (truncation), append
-                const int t_new = (ctx_b - 1) % kBS;
-                const long long src = ((long long)cur.b * a.Hkv + cur.h) * D + lane * 8;
-                float kx[8], vx[8];
-                if (a.q_f16) {
-                    load8(reinterpret_cast<const __half*>(a.k_new) + src, kx);
-                    load8(reinterpret_cast<const __half*>(a.v_new) + src, vx);
-                } else {
-                    load8(reinterpret_cast<const float*>(a.k_new) + src, kx);
-                    load8(reinterpret_cast<const float*>(a.v_new) + src, vx);
-                }
-                const float4* cs =
-                    reinterpret_cast<const float4*>(a.cos_sin + ((long long)(ctx_b - 1) * (D / 2) + lane * 4) * 2);
-#pragma unroll
-                for (int pr = 0; pr < 2; ++pr) {
-                    const float4 c4 = __ldg(cs + pr);
-                    rope_pair(kx[4 * pr], kx[4 * pr + 1], c4.x, c4.y, kx[4 * pr], kx[4 * pr + 1]);
-                    rope_pair(kx[4 * pr + 2], kx[4 * pr + 3], c4.z, c4.w, kx[4 * pr + 2], kx[4 * pr + 3]);
-                }
-                uint32_t kw[4], vw[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    kw[j] = (uint32_t)f32_to_f16_trunc(kx[2 * j]) | ((uint32_t)f32_to_f16_trunc(kx[2 * j + 1]) << 16);
-                    vw[j] = (uint32_t)f32_to_f16_trunc(vx[2 * j]) | ((uint32_t)f32_to_f16_trunc(vx[2 * j + 1]) << 16);
-                }
-                const uint4 k4 = make_uint4(kw[0], kw[1], kw[2], kw[3]);
-                const uint4 v4 = make_uint4(vw[0], vw[1], vw[2], vw[3]);
-                *reinterpret_cast<uint4*>(sl + swz(lane / 8, t_new, lane % 8)) = k4;
-                *reinterpret_cast<uint4*>(sl + swz(lane / 8, kBS + t_new, lane % 8)) = v4;
-                const long long row0 = ((long long)blk * a.L + a.layer) * (2 * kBS);
-                *reinterpret_cast<uint4*>(a.kv + ((row0 + t_new) * a.Hkv + cur.h) * D + lane * 8) = k4;
-                *reinterpret_cast<uint4*>(a.kv + ((row0 + kBS + t_new) * a.Hkv + cur.h) * D + lane * 8) = v4;
-            }
+            if (ROPE && blk_ok && p == seg.c.np - 1 && lane < LW)
+                append_new_token<D>(sl, a.kv, a.k_new, a.v_new, a.cos_sin, a.q_f16, blk, a.L, a.layer, a.Hkv,
+                                    seg.c.b, seg.c.h, ctx_b, lane);
             if (n_valid < kBS) {
                 // V rows past the context may hold any bits (NaN, inf); zero them
                 // so that 0-probability tokens contribute exactly 0
@@ -316,17 +575,28 @@ __global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
             if (ROPE || n_valid < kBS) __syncwarp();
 
             // ---- S^T = K . Q^T ----------------------------------------------------
+            // two independent accumulator chains (hi and lo query parts, or even and
+            // odd k-steps), added at the end: half the dependent MMA latency
             float s[4] = {0.f, 0.f, 0.f, 0.f};
             {
+                float s2[4] = {0.f, 0.f, 0.f, 0.f};
                 const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
                 const int csel = lane >> 4;
 #pragma unroll
                 for (int kk = 0; kk < KS; ++kk) {
                     uint32_t af[4];
                     ldsm_x4(sl_s + swz(kk / 4, row, (kk % 4) * 2 + csel), af);
-                    mma16816(s, af, qb[kk][0], qb[kk][1]);
-                    if constexpr (QSPLIT) mma16816(s, af, ql[kk][0], ql[kk][1]);
+                    if constexpr (QSPLIT) {
+                        mma16816(s, af, qb[kk][0], qb[kk][1]);
+                        mma16816(s2, af, ql[kk][0], ql[kk][1]);
+                    } else if (kk & 1) {
+                        mma16816(s2, af, qb[kk][0], qb[kk][1]);
+                    } else {
+                        mma16816(s, af, qb[kk][0], qb[kk][1]);
+                    }
                 }
+#pragma unroll
+                for (int i = 0; i < 4; ++i) s[i] += s2[i];
             }
             // ---- online softmax on the fragment -----------------------------------
             const bool ok0 = qr < n_valid, ok1 = qr + 8 < n_valid;
@@ -334,9 +604,9 @@ __global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
             const float s10 = ok1 ? s[2] * a.qscale : -INFINITY, s11 = ok1 ? s[3] * a.qscale : -INFINITY;
             float c0 = fmaxf(s00, s10), c1 = fmaxf(s01, s11);
 #pragma unroll
-            for (int off = 4; off < 32; off <<= 1) {
-                c0 = fmaxf(c0, __shfl_xor_sync(FULL, c0, off));
-                c1 = fmaxf(c1, __shfl_xor_sync(FULL, c1, off));
+            for (int sh = 4; sh < 32; sh <<= 1) {
+                c0 = fmaxf(c0, __shfl_xor_sync(FULL, c0, sh));
+                c1 = fmaxf(c1, __shfl_xor_sync(FULL, c1, sh));
             }
             if (c0 > m0 + 8.0f) {
                 const float al = exp2f(m0 - c0);
@@ -366,9 +636,9 @@ __global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
             const uint32_t pb1 = movmatrix_trans(pack_h2(p10, p11));  // tokens 8-15
             uint32_t pl0 = 0u, pl1 = 0u;  // fp32 outputs: the remainders of the fp16 roundings
             if constexpr (PSPLIT) {
-                const float2 h0 = unpack_h2(pack_h2(p00, p01)), h1 = unpack_h2(pack_h2(p10, p11));
-                pl0 = movmatrix_trans(pack_h2(p00 - h0.x, p01 - h0.y));
-                pl1 = movmatrix_trans(pack_h2(p10 - h1.x, p11 - h1.y));
+                const float2 e0 = unpack_h2(pack_h2(p00, p01)), e1 = unpack_h2(pack_h2(p10, p11));
+                pl0 = movmatrix_trans(pack_h2(p00 - e0.x, p01 - e0.y));
+                pl1 = movmatrix_trans(pack_h2(p10 - e1.x, p11 - e1.y));
             }
 
             // ---- O^T += V^T . P^T --------------------------------------------------
@@ -384,73 +654,117 @@ __global__ void __launch_bounds__(kNW * 32, kMmaMinCtas)
                 }
             }
             __syncwarp();
-
-            if (k + RING < nu) {
+            ++mine;
+            if (ic_ok) {
                 fence_proxy_async_smem();
-                issue(k + RING);
+                issue_one(true);
             }
-
-            // the next page ends a cut segment of this pair: read the pair's
-            // arrival counter now, so the arrival's compare-and-swap finds it
-            if (lane == 0 && k + 1 < nu && cur.p + 1 < cur.np && (cur.p + 2 == cur.np || k + 2 == nu) &&
-                !(seg_start_p == 0 && cur.p + 2 == cur.np))
-                ctr_hint = ld_relaxed_u64(a.counters + 1 + (long long)cur.b * a.Hkv + cur.h);
-
-            const bool seg_end = (cur.p == cur.np - 1) || (k == nu - 1);
-            if (seg_end) {
-                float lt0 = l0, lt1 = l1;
-#pragma unroll
-                for (int off = 4; off < 32; off <<= 1) {
-                    lt0 += __shfl_xor_sync(FULL, lt0, off);
-                    lt1 += __shfl_xor_sync(FULL, lt1, off);
-                }
-                const bool whole = seg_start_p == 0 && cur.p == cur.np - 1;
-                const long long slot_id = seg_first ? 2 * cid : 2 * cid + 1;
-#pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const int g = hh ? h1 : h0;
-                    if (g >= G) continue;
-                    const float mg = hh ? m1 : m0, lg = hh ? lt1 : lt0;
-                    const long long head = (long long)cur.b * a.H + (long long)cur.h * G + g;
-                    if (whole) {
-                        const float inv = lg > 0.f ? 1.0f / lg : 0.f;
-#pragma unroll
-                        for (int j = 0; j < KS; ++j) {
-                            const float x0 = o[j][hh] * inv, x1 = o[j][2 + hh] * inv;
-                            const long long e0 = head * D + j * 16 + qr;
-                            if (a.out_f16) {
-                                reinterpret_cast<__half*>(a.out)[e0] = __float2half_rn(x0);
-                                reinterpret_cast<__half*>(a.out)[e0 + 8] = __float2half_rn(x1);
-                            } else {
-                                reinterpret_cast<float*>(a.out)[e0] = x0;
-                                reinterpret_cast<float*>(a.out)[e0 + 8] = x1;
-                            }
-                        }
-                        if (a.lse && qr == 0) a.lse[head] = lg > 0.f ? (mg + log2f(lg)) * kLn2 : -INFINITY;
-                    } else {
-                        float* dst = a.ws_o + (slot_id * G + g) * D;
-#pragma unroll
-                        for (int j = 0; j < KS; ++j) {
-                            dst[j * 16 + qr] = o[j][hh];
-                            dst[j * 16 + qr + 8] = o[j][2 + hh];
-                        }
-                        if (qr == 0) {
-                            a.ws_ml[(slot_id * G + g) * 2] = mg;
-                            a.ws_ml[(slot_id * G + g) * 2 + 1] = lg;
-                        }
-                    }
-                }
-                if (!whole)
-                    merge_if_last<D, G>(a, cur.b, cur.h, u0 + k - cur.p, cur.np, chunk, lane, ctr_hint);
-                __syncwarp();
-                seg_open = false;
-            }
-            if (k + 1 < nu) cursor_next<ROPE>(cur, a);
         }
-        kg += nu;
-        cid = NC > W ? grab_chunk(a, W, NC, lane) : NC;
+
+        // ---- segment end: merge the warps' states in shared memory --------------
+        {
+            float lt0 = l0, lt1 = l1;
+#pragma unroll
+            for (int sh = 4; sh < 32; sh <<= 1) {
+                lt0 += __shfl_xor_sync(FULL, lt0, sh);
+                lt1 += __shfl_xor_sync(FULL, lt1, sh);
+            }
+            float* mo = merge_o + warp * G * OST;
+            float* mml = merge_ml + warp * G * 2;
+            if (h0 < G) {
+#pragma unroll
+                for (int j = 0; j < KS; ++j) {
+                    mo[h0 * OST + j * 16 + qr] = o[j][0];
+                    mo[h0 * OST + j * 16 + qr + 8] = o[j][2];
+                }
+                if (qr == 0) {
+                    mml[h0 * 2] = m0;
+                    mml[h0 * 2 + 1] = lt0;
+                }
+            }
+            if (h1 < G) {
+#pragma unroll
+                for (int j = 0; j < KS; ++j) {
+                    mo[h1 * OST + j * 16 + qr] = o[j][1];
+                    mo[h1 * OST + j * 16 + qr + 8] = o[j][3];
+                }
+                if (qr == 0) {
+                    mml[h1 * 2] = m1;
+                    mml[h1 * 2 + 1] = lt1;
+                }
+            }
+        }
+        __syncthreads();
+        if (s_abort) {  // every warp sees the same flag after the barrier
+            drain();
+            return;
+        }
+        const long long slot_id = seg.c.ps <= u0 ? 2 * cid : 2 * cid + 1;
+        constexpr int ITEMS = G * D / 4;  // (head, 4 dims)
+        for (int it = threadIdx.x; it < ITEMS; it += kNW * 32) {
+            const int g = it / (D / 4), c4 = it % (D / 4);
+            float M = -INFINITY;
+            float mw[kNW];
+#pragma unroll
+            for (int w = 0; w < kNW; ++w) {
+                mw[w] = merge_ml[(w * G + g) * 2];
+                M = fmaxf(M, mw[w]);
+            }
+            float L = 0.f;
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int w = 0; w < kNW; ++w) {
+                    if (mw[w] == -INFINITY) continue;
+                    const float sc = exp2f(mw[w] - M);
+                    L += merge_ml[(w * G + g) * 2 + 1] * sc;
+                    const float4 x = *reinterpret_cast<const float4*>(merge_o + (w * G + g) * OST + c4 * 4);
+                    acc.x += x.x * sc;
+                    acc.y += x.y * sc;
+                    acc.z += x.z * sc;
+                    acc.w += x.w * sc;
+                }
+            }
+            const long long head = (long long)seg.c.b * a.H + (long long)seg.c.h * G + g;
+            if (whole) {
+                const float inv = L > 0.f ? 1.0f / L : 0.f;
+                const float v4[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+                if (a.out_f16) {
+                    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(a.out) + head * D + c4 * 4) =
+                        make_uint2(pack_h2(v4[0], v4[1]), pack_h2(v4[2], v4[3]));
+                } else {
+                    *reinterpret_cast<float4*>(reinterpret_cast<float*>(a.out) + head * D + c4 * 4) =
+                        make_float4(v4[0], v4[1], v4[2], v4[3]);
+                }
+                if (a.lse && c4 == 0) a.lse[head] = L > 0.f ? (M + log2f(L)) * kLn2 : -INFINITY;
+            } else {
+                *reinterpret_cast<float4*>(a.ws_o + (slot_id * G + g) * D + c4 * 4) = acc;
+                if (c4 == 0) *reinterpret_cast<float2*>(a.ws_ml + (slot_id * G + g) * 2) = make_float2(M, L);
+            }
+        }
+        if (!whole) {
+            const MergeArgs ma = {a.counters, a.ws_o, a.ws_ml, a.out, a.lse, a.H, a.Hkv, a.out_f16, a.epoch};
+            arrive_cut_pair<D, G>(ma, chunk, seg.c.b, seg.c.h, seg.c.np, seg.c.ps, ctr_hint, &s_last);
+        }
+        __syncthreads();  // the merge area is free for the next segment
+        next_segment<ROPE, PAD>(seg, a, u1);
     }
-    signal_done(a, lane, &cta_done);
+
+    // ---- split-context completion signal: once every CTA has stored its outputs ----
+    if (a.sig.world != 0) {
+        __threadfence();  // this thread's outputs, before the CTA counts itself
+        __syncthreads();
+    }
+    if (a.sig.world != 0 && threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(a.sig.done, 1u) == gridDim.x - 1) {
+            *reinterpret_cast<volatile unsigned*>(a.sig.done) = 0u;  // for the next launch
+            __threadfence_system();
+            for (int r = 0; r < a.sig.world; ++r)
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig.flags[r] + a.sig.rank), "r"(a.sig.epoch)
+                             : "memory");
+        }
+    }
 }
 
 template <int D, int G, int RING, bool ROPE, bool QSPLIT, bool PSPLIT>
@@ -460,7 +774,7 @@ struct MmaLauncher {
         if (device < 0 || device >= 64) return 1;
         if (cache[device] == 0) {
             auto kern = decode_mma_kernel<D, G, RING, ROPE, QSPLIT, PSPLIT>;
-            const size_t smem = mma_smem_bytes<RING, D>();
+            const size_t smem = mma_smem_bytes<RING, D, G>();
             cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
             int n = 0;
             cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kNW * 32, smem);
@@ -468,9 +782,8 @@ struct MmaLauncher {
         }
         return cache[device];
     }
-    static long long workers(int device) {
-        return (long long)device_sm_count(device) * blocks_per_sm(device) * kNW;
-    }
+    // workers: one per CTA
+    static long long workers(int device) { return (long long)device_sm_count(device) * blocks_per_sm(device); }
     static cudaError_t launch(const DecodeDesc& d, cudaStream_t st) {
         int dev = 0;
         cudaGetDevice(&dev);
@@ -479,8 +792,17 @@ struct MmaLauncher {
         const CUtensorMap map = make_kv_tensor_map(d, true, &err);
         if (err != cudaSuccess) return err;
         TmaArgs a = make_tma_args(d, W, G, D);
-        return launch_pdl(decode_mma_kernel<D, G, RING, ROPE, QSPLIT, PSPLIT>, (int)(W / kNW), mma_smem_bytes<RING, D>(), st,
-                          map, a);
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)W);
+        cfg.blockDim = dim3(kNW * 32);
+        cfg.dynamicSmemBytes = mma_smem_bytes<RING, D, G>();
+        cfg.stream = st;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        return cudaLaunchKernelEx(&cfg, decode_mma_kernel<D, G, RING, ROPE, QSPLIT, PSPLIT>, map, a);
     }
 };
 

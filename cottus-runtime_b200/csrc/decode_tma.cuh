@@ -41,16 +41,7 @@ namespace cb200 {
 
 constexpr int kBS = 16;   // tokens per page on the fast path
 constexpr int kNW = 4;    // worker warps per CTA
-constexpr int kMinChunk = 8;  // fewest pages in a chunk (limits partials on tiny batches)
-#ifndef CB200_CHUNKS_PER_WORKER
-#define CB200_CHUNKS_PER_WORKER 1
-#endif
-// Chunks per worker on average: each worker takes one static chunk, then
-// grabs more from a queue, so warps that stream slower take less work.
-// Measured on B200 (Llama-3-8B and 131k-context shapes): 1 is fastest;
-// 2, 3, 4 lose 10-45% because every chunk restarts the page ring from empty
-// and cuts its pairs into extra partials.
-constexpr int kChunksPerWorker = CB200_CHUNKS_PER_WORKER;
+constexpr int kMinChunk = 8;  // fewest pages in a warp's chunk (limits partials on tiny batches)
 
 struct TmaArgs {
     void* out;
@@ -61,7 +52,7 @@ struct TmaArgs {
     float* lse;
     float* ws_o;
     float* ws_ml;
-    unsigned long long* counters;  // chunk queue word, then [B * Hkv] arrival counters tagged with `epoch`
+    unsigned long long* counters;  // a reserved word, then [B * Hkv] arrival counters tagged with `epoch`
     uint32_t* status;
     const void* k_new;
     const void* v_new;
@@ -171,13 +162,19 @@ struct TransposeReduce {
     }
 };
 
+// A position in the unit order.  Units of a pair may be followed by `pad`
+// virtual units (no page: they only weigh a pair's fixed cost in the
+// partition into chunks); cursors visit real pages only, and ps is the unit
+// index of the current pair's first unit.
 struct Cursor {
     int b, h, p, np, n;  // sequence, kv head, page, pages of b, context of b
+    long long ps;
 };
 
 template <bool ROPE>
-__device__ __forceinline__ void cursor_next(Cursor& c, const TmaArgs& a) {
+__device__ __forceinline__ void cursor_next(Cursor& c, const TmaArgs& a, int pad = 0) {
     if (++c.p == c.np) {
+        c.ps += c.np + pad;
         c.p = 0;
         if (++c.h == a.Hkv) {
             c.h = 0;
@@ -212,14 +209,15 @@ __device__ __forceinline__ void zero_empty_sequences(const TmaArgs& a, long long
 // (sequence, kv head, page) of unit u (< total units): a warp-wide prefix
 // scan over the sequences' page counts, then division by the page count.
 template <bool ROPE>
-__device__ __forceinline__ Cursor locate_unit(const TmaArgs& a, long long u, int lane) {
+__device__ __forceinline__ Cursor locate_unit(const TmaArgs& a, long long u, int lane, int pad = 0) {
     constexpr unsigned FULL = 0xffffffffu;
     long long base = 0;
     int found_b = -1;
     long long found_excl = 0;
     for (int bb = 0; bb < a.B && found_b < 0; bb += 32) {
         const int b = bb + lane;
-        const long long units = b < a.B ? (long long)seq_pages<ROPE>(a, b) * a.Hkv : 0;
+        const int pg = b < a.B ? seq_pages<ROPE>(a, b) : 0;
+        const long long units = pg > 0 ? (long long)(pg + pad) * a.Hkv : 0;
         long long incl = units;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -243,8 +241,13 @@ __device__ __forceinline__ Cursor locate_unit(const TmaArgs& a, long long u, int
     c.b = found_b;
     c.np = np;
     c.n = n_b;
-    c.h = (int)(r / np);
-    c.p = (int)(r % np);
+    c.h = (int)(r / (np + pad));
+    c.p = (int)(r % (np + pad));
+    c.ps = found_excl + (long long)c.h * (np + pad);
+    if (c.p >= np) {  // a virtual unit: the next real one is page 0 of the next pair
+        c.p = np - 1;
+        cursor_next<ROPE>(c, a, pad);
+    }
     return c;
 }
 
@@ -267,14 +270,15 @@ struct CachedHit {
     int b, i, src;
     long long excl;
 };
-__device__ __forceinline__ CachedHit locate_cached(const int (&pg)[kPlanRegs], long long u, int Hkv, int lane) {
+__device__ __forceinline__ CachedHit locate_cached(const int (&pg)[kPlanRegs], long long u, int Hkv, int lane,
+                                                  int pad = 0) {
     constexpr unsigned FULL = 0xffffffffu;
     CachedHit h = {-1, 0, 0, 0};
     long long base = 0;
 #pragma unroll
     for (int i = 0; i < kPlanRegs; ++i) {
         if (h.b >= 0) break;
-        const long long units = (long long)pg[i] * Hkv;
+        const long long units = pg[i] > 0 ? (long long)(pg[i] + pad) * Hkv : 0;
         long long incl = units;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -295,45 +299,44 @@ __device__ __forceinline__ CachedHit locate_cached(const int (&pg)[kPlanRegs], l
     return h;
 }
 
-template <int D, bool ROPE>
-__device__ __forceinline__ WorkerPlan plan_worker(const TmaArgs& a, long long w, long long W, int lane) {
-    constexpr unsigned FULL = 0xffffffffu;
-    WorkerPlan pl;
-    if (a.B > 32 * kPlanRegs) {
-        long long total_pages = 0;
-        for (int b = lane; b < a.B; b += 32) total_pages += seq_pages<ROPE>(a, b);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) total_pages += __shfl_xor_sync(FULL, total_pages, o);
-        pl.U = total_pages * a.Hkv;
-        pl.chunk = max((pl.U + W * kChunksPerWorker - 1) / (W * kChunksPerWorker), (long long)kMinChunk);
-        pl.u0 = min(w * pl.chunk, pl.U);
-        pl.u1 = min(pl.u0 + pl.chunk, pl.U);
-        zero_empty_sequences<D, ROPE>(a, w, W, lane);
-        if (pl.u0 < pl.u1) pl.cur = locate_unit<ROPE>(a, pl.u0, lane);
-        return pl;
-    }
+// Worker w of W (a warp, or a whole CTA whose warps share the chunk): its
+// chunk is at least min_chunk units; zero_fill selects the one warp of the
+// worker that writes the zero rows of empty sequences.
+// Per-lane snapshot of the page counts and context lengths of sequences
+// lane, lane + 32, ... (batches up to kPlanRegs * 32).
+struct PlanRegs {
     int pg[kPlanRegs], cx[kPlanRegs];
-    long long total = 0;
+};
+template <bool ROPE>
+__device__ __forceinline__ PlanRegs load_plan_regs(const TmaArgs& a, int lane) {
+    PlanRegs r;
 #pragma unroll
     for (int i = 0; i < kPlanRegs; ++i) {
         const int b = lane + 32 * i;
-        cx[i] = 0;
-        pg[i] = b < a.B ? seq_pages<ROPE>(a, b, &cx[i]) : 0;
-        total += pg[i];
+        r.cx[i] = 0;
+        r.pg[i] = b < a.B ? seq_pages<ROPE>(a, b, &r.cx[i]) : 0;
     }
+    return r;
+}
+template <bool ROPE>
+__device__ __forceinline__ bool same_plan_regs(const PlanRegs& x, const PlanRegs& y) {
+    bool same = true;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(FULL, total, o);
-    pl.U = total * a.Hkv;
-    pl.chunk = max((pl.U + W * kChunksPerWorker - 1) / (W * kChunksPerWorker), (long long)kMinChunk);
-    pl.u0 = min(w * pl.chunk, pl.U);
-    pl.u1 = min(pl.u0 + pl.chunk, pl.U);
-    // worker i < kPlanRegs zero-fills the empty sequences among 32i .. 32i+31
+    for (int i = 0; i < kPlanRegs; ++i) same = same && x.pg[i] == y.pg[i] && x.cx[i] == y.cx[i];
+    return __all_sync(0xffffffffu, same);
+}
+
+// Worker w < kPlanRegs writes the zero rows of the empty sequences among
+// 32w .. 32w + 31 (and reports the invalid lengths among them).
+template <int D, bool ROPE>
+__device__ __forceinline__ void zero_fill_from_regs(const TmaArgs& a, const PlanRegs& r, long long w, int lane) {
+    constexpr unsigned FULL = 0xffffffffu;
 #pragma unroll
     for (int i = 0; i < kPlanRegs; ++i) {
         if (w != i) continue;
         const int b = lane + 32 * i;
-        unsigned empty = __ballot_sync(FULL, b < a.B && pg[i] == 0);
-        if (b < a.B && pg[i] == 0 && (ROPE || cx[i] != 0))
+        unsigned empty = __ballot_sync(FULL, b < a.B && r.pg[i] == 0);
+        if (b < a.B && r.pg[i] == 0 && (ROPE || r.cx[i] != 0))
             report(a.status, ROPE ? COTTUS_STATUS_BAD_POSITION : COTTUS_STATUS_BAD_CONTEXT);
         const long long nel = (long long)a.H * D;
         while (empty) {
@@ -349,65 +352,100 @@ __device__ __forceinline__ WorkerPlan plan_worker(const TmaArgs& a, long long w,
                 for (int e = lane; e < a.H; e += 32) a.lse[bb * a.H + e] = -INFINITY;
         }
     }
+}
+
+// The plan of worker w from a snapshot (reads only: the lengths of the
+// sequences after the first one, when the chunk starts in a virtual unit).
+template <bool ROPE>
+__device__ __forceinline__ WorkerPlan plan_from_regs(const TmaArgs& a, const PlanRegs& r, long long w,
+                                                     long long W, int lane, long long min_chunk, int pad) {
+    constexpr unsigned FULL = 0xffffffffu;
+    WorkerPlan pl;
+    long long total = 0;
+#pragma unroll
+    for (int i = 0; i < kPlanRegs; ++i) total += r.pg[i] > 0 ? r.pg[i] + pad : 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(FULL, total, o);
+    pl.U = total * a.Hkv;
+    pl.chunk = max((pl.U + W - 1) / W, min_chunk);
+    pl.u0 = min(w * pl.chunk, pl.U);
+    pl.u1 = min(pl.u0 + pl.chunk, pl.U);
     if (pl.u0 >= pl.u1) return pl;
     // locate u0 from the cached page counts
-    const CachedHit hit = locate_cached(pg, pl.u0, a.Hkv, lane);
+    const CachedHit hit = locate_cached(r.pg, pl.u0, a.Hkv, lane, pad);
     int fnp = 0, fn = 0;
 #pragma unroll
     for (int i = 0; i < kPlanRegs; ++i) {  // register arrays are indexed with constants only
-        const int np_i = __shfl_sync(FULL, pg[i], hit.src), n_i = __shfl_sync(FULL, cx[i], hit.src);
+        const int np_i = __shfl_sync(FULL, r.pg[i], hit.src), n_i = __shfl_sync(FULL, r.cx[i], hit.src);
         if (i == hit.i) {
             fnp = np_i;
             fn = n_i;
         }
     }
-    const int fb = hit.b;
-    const long long fex = hit.excl;
-    const long long r = pl.u0 - fex;
-    pl.cur.b = fb;
+    const long long rr = pl.u0 - hit.excl;
+    pl.cur.b = hit.b;
     pl.cur.np = fnp;
     pl.cur.n = fn;
-    pl.cur.h = (int)(r / fnp);
-    pl.cur.p = (int)(r % fnp);
+    pl.cur.h = (int)(rr / (fnp + pad));
+    pl.cur.p = (int)(rr % (fnp + pad));
+    pl.cur.ps = hit.excl + (long long)pl.cur.h * (fnp + pad);
+    if (pl.cur.p >= fnp) {  // a virtual unit: the next real one is page 0 of the next pair
+        pl.cur.p = fnp - 1;
+        cursor_next<ROPE>(pl.cur, a, pad);
+    }
     return pl;
 }
 
-// Next chunk id for this warp: chunks 0..W-1 are taken statically by
-// workers 0..W-1, chunks W.. are handed out by a ticket counter (one word
-// at the start of the workspace, zero at launch start).  Every warp stops
-// at its first ticket past the last chunk, so exactly W such tickets are
-// drawn; the warp that draws the last of them resets the counter to zero
-// for the next launch on this workspace.  A plain atomicAdd per grab keeps
-// the queue contention-free even when every warp grabs at once.
-__device__ __forceinline__ long long grab_chunk(const TmaArgs& a, long long W, long long NC, int lane) {
-    long long id = 0;
-    if (lane == 0) {
-        const long long ticket = (long long)atomicAdd(a.counters, 1ull);
-        const long long ndyn = NC > W ? NC - W : 0;
-        id = W + ticket;
-        if (ticket == ndyn + W - 1) atomicExch(a.counters, 0ull);
+// With pad > 0 every pair is followed by pad virtual units (see Cursor);
+// the cursor returned is at the first real unit at or after u0 (which may
+// lie at or past u1 when the chunk holds only virtual units).
+template <int D, bool ROPE>
+__device__ __forceinline__ WorkerPlan plan_worker(const TmaArgs& a, long long w, long long W, int lane,
+                                                  long long min_chunk = kMinChunk, bool zero_fill = true,
+                                                  int pad = 0) {
+    constexpr unsigned FULL = 0xffffffffu;
+    WorkerPlan pl;
+    if (a.B > 32 * kPlanRegs) {
+        long long total_pages = 0;
+        for (int b = lane; b < a.B; b += 32) {
+            const int pg = seq_pages<ROPE>(a, b);
+            total_pages += pg > 0 ? pg + pad : 0;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) total_pages += __shfl_xor_sync(FULL, total_pages, o);
+        pl.U = total_pages * a.Hkv;
+        pl.chunk = max((pl.U + W - 1) / W, min_chunk);
+        pl.u0 = min(w * pl.chunk, pl.U);
+        pl.u1 = min(pl.u0 + pl.chunk, pl.U);
+        if (zero_fill) zero_empty_sequences<D, ROPE>(a, w, W, lane);
+        if (pl.u0 < pl.u1) pl.cur = locate_unit<ROPE>(a, pl.u0, lane, pad);
+        return pl;
     }
-    return __shfl_sync(0xffffffffu, id, 0);
+    const PlanRegs r = load_plan_regs<ROPE>(a, lane);
+    if (zero_fill) zero_fill_from_regs<D, ROPE>(a, r, w, lane);
+    return plan_from_regs<ROPE>(a, r, w, W, lane, min_chunk, pad);
 }
 
 // Pages of a worker's static chunk warmed in L2 before the wait for the
 // preceding kernel.
 constexpr int kWarmPages = 2;
 
-// L2 prefetch (TMA, nothing written) of the first pages (at most
-// kWarmPages, within its first (sequence, kv head) segment) of this
-// worker's static chunk, issued before griddepcontrol.wait so that a launch
-// made resident during the preceding kernel's tail streams its first pages
-// meanwhile.  The chunk is located as plan_worker locates it, from one
-// snapshot of the lengths that the preceding kernel may still be writing:
-// a stale snapshot only warms the wrong lines (every index is checked
-// against the snapshot and the table's bounds, block ids against the pool,
-// the tensor map bounds the box, and the real loads come after the wait;
-// L2 is the point of coherence, so nothing stale can be read from it).
-// Batches beyond kPlanRegs * 32 sequences are not warmed.
+// L2 prefetch (TMA, nothing written) of units u0 + first and
+// u0 + first + stride of this worker's chunk (the first pages the warp will
+// load), issued before griddepcontrol.wait so that a launch made resident
+// during the preceding kernel's tail streams its first pages meanwhile.  The
+// chunk is located as plan_worker locates it, from one snapshot of the
+// lengths that the preceding kernel may still be writing: a stale snapshot
+// only warms the wrong lines (every index is checked against the snapshot
+// and the table's bounds, block ids against the pool, the tensor map bounds
+// the box, and the real loads come after the wait; L2 is the point of
+// coherence, so nothing stale can be read from it).  Batches beyond
+// kPlanRegs * 32 sequences are not warmed.
 template <bool ROPE>
 __device__ __forceinline__ void warm_first_pages(const TmaArgs& a, const CUtensorMap* map, long long w,
-                                                 long long W, int lane, int boxes, int box_elems) {
+                                                 long long W, int lane, int boxes, int box_elems,
+                                                 long long min_chunk = kMinChunk, int first = 0, int stride = 1,
+                                                 int pad = 0) {
     constexpr unsigned FULL = 0xffffffffu;
     if (kWarmPages == 0 || a.B > 32 * kPlanRegs) return;
     int pg[kPlanRegs];
@@ -416,28 +454,28 @@ __device__ __forceinline__ void warm_first_pages(const TmaArgs& a, const CUtenso
     for (int i = 0; i < kPlanRegs; ++i) {
         const int b = lane + 32 * i;
         pg[i] = b < a.B ? seq_pages<ROPE>(a, b) : 0;
-        total += pg[i];
+        total += pg[i] > 0 ? pg[i] + pad : 0;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(FULL, total, o);
     const long long U = total * a.Hkv;
-    const long long chunk = max((U + W * kChunksPerWorker - 1) / (W * kChunksPerWorker), (long long)kMinChunk);
-    const long long u0 = w * chunk;
-    if (u0 >= U) return;
-    const CachedHit hit = locate_cached(pg, u0, a.Hkv, lane);
-    int np = 0;
+    const long long chunk = max((U + W - 1) / W, min_chunk);
+    const long long u0 = w * chunk, u1 = min(u0 + chunk, U);
+#pragma unroll 1
+    for (int i = 0; i < kWarmPages; ++i) {
+        const long long u = u0 + first + (long long)i * stride;
+        if (u >= u1) return;
+        const CachedHit hit = locate_cached(pg, u, a.Hkv, lane, pad);
+        int np = 0;
 #pragma unroll
-    for (int i = 0; i < kPlanRegs; ++i) {
-        const int np_i = __shfl_sync(FULL, pg[i], hit.src);
-        if (i == hit.i) np = np_i;
-    }
-    if (lane != 0 || hit.b < 0 || hit.b >= a.B || np <= 0) return;
-    const long long r = u0 - hit.excl;
-    const int h = (int)(r / np);
-    int p = (int)(r % np);
-    if (h >= a.Hkv) return;
-    const int pend = (int)min((long long)np, (long long)p + min((long long)kWarmPages, U - u0));
-    for (; p < pend && p < a.maxb; ++p) {
+        for (int j = 0; j < kPlanRegs; ++j) {
+            const int np_j = __shfl_sync(FULL, pg[j], hit.src);
+            if (j == hit.i) np = np_j;
+        }
+        if (lane != 0 || hit.b < 0 || hit.b >= a.B || np <= 0) continue;
+        const long long r = u - hit.excl;
+        const int h = (int)(r / (np + pad)), p = (int)(r % (np + pad));
+        if (h >= a.Hkv || p >= np || p >= a.maxb) continue;  // past the table, or a virtual unit
         const int blk = a.bt[(long long)hit.b * a.maxb + p];
         if (blk >= 0 && (long long)blk < a.num_blocks)
             for (int q = 0; q < boxes; ++q) tma_prefetch_l2_3d(map, q * box_elems, h, (blk * a.L + a.layer) * (2 * kBS));
@@ -584,16 +622,13 @@ __global__ void __launch_bounds__(kNW * 32)
     const int i0 = (lq * N) / LW;   // first partial index this lane holds after the reduction
     const int gl = i0 / STEPS;      // the head this lane scores
 
-    long long cid = w < NC ? w : (NC > W ? grab_chunk(a, W, NC, lane) : NC);
+    long long cid = w < NC ? w : NC;
     Cursor cur = pl.cur;
-    bool have_cur = w < NC;
     int kg = 0;  // units consumed by this warp so far (ring slot / phase counter)
 
-    while (cid < NC) {
+    while (cid < NC) {  // one static chunk per warp
         const long long u0 = cid * chunk, u1 = min(u0 + chunk, U);
         const int nu = (int)(u1 - u0);
-        if (!have_cur) cur = locate_unit<ROPE>(a, u0, lane);
-        have_cur = false;
 
         // ---- TMA issue: lane 0 owns the issue cursor; the block id of the next
         // unit to issue is loaded one page ahead so its latency hides behind math.
@@ -879,7 +914,7 @@ __global__ void __launch_bounds__(kNW * 32)
             if (k + 1 < nu) cursor_next<ROPE>(cur, a);
         }
         kg += nu;
-        cid = NC > W ? grab_chunk(a, W, NC, lane) : NC;
+        cid = NC;
     }
     signal_done(a, lane, &cta_done);
 }
@@ -892,7 +927,7 @@ int device_sm_count(int device);
 unsigned next_epoch();
 
 // Upper bound on the number of chunks of a launch with W workers.
-inline long long max_chunks(long long W) { return W * kChunksPerWorker + 1; }
+inline long long max_chunks(long long W) { return W + 1; }
 
 // Launch with programmatic stream serialization: the kernel may begin its
 // prologue while the previous kernel of the stream drains; it waits
@@ -913,9 +948,9 @@ inline cudaError_t launch_pdl(Kern kern, int grid, size_t smem, cudaStream_t st,
     return cudaLaunchKernelEx(&cfg, kern, map, a);
 }
 
-// Kernel arguments of one launch; the workspace holds the chunk queue word
-// and the pair counters, then 2 partial slots per chunk of G x D outputs
-// and G x (m, l).
+// Kernel arguments of one launch; the workspace holds a reserved word and
+// the pair counters, then 2 partial slots per chunk of G x D outputs and
+// G x (m, l).
 inline TmaArgs make_tma_args(const DecodeDesc& d, long long W, int G, int D) {
     TmaArgs a;
     a.out = d.out;

@@ -344,13 +344,26 @@ cudaError_t launch_rope_single(float* out, const float* in, const float* host_co
 }
 
 // ---------------------------------------------------------------------------
-// Split-KV merge of (normalised partial, lse) pairs.  One warp per head.
+// Split-KV merge of (normalised partial, lse) pairs.  One warp per head;
+// up to kMergeParts parts with merge_head_parts (all loads in flight at
+// once), more with the same arithmetic in a loop over the parts.
 // ---------------------------------------------------------------------------
 __global__ void lse_combine_kernel(void* out, int out_f16, float* lse_out, const float* part_out,
                                    const float* part_lse, int P, long long heads, int D) {
     const long long hw = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (hw >= heads) return;
+    if (P <= kMergeParts) {
+        const float* lse[kMergeParts];
+        const float* row[kMergeParts];
+#pragma unroll
+        for (int p = 0; p < kMergeParts; ++p) {
+            lse[p] = part_lse + (long long)(p < P ? p : 0) * heads;
+            row[p] = part_out + (long long)(p < P ? p : 0) * heads * D;
+        }
+        merge_head_parts(lse, row, P, hw, D, lane, out, out_f16, lse_out);
+        return;
+    }
     float M = -INFINITY;
     for (int p = 0; p < P; ++p) M = fmaxf(M, part_lse[p * heads + hw]);
     float S = 0.f;

@@ -69,6 +69,7 @@ Layout layout_of(int world, long long heads, int head_dim) {
     return l;
 }
 
+static_assert(kMaxPeers == kMergeParts, "one merge part per rank");
 struct PeerSlots {
     const float* part[kMaxPeers];
     const float* lse[kMaxPeers];
@@ -90,8 +91,8 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
-// One warp per (sequence, head); lanes over head_dim.  Same operations, in
-// the same order, as lse_combine_kernel over parts 0..world-1.
+// One warp per (sequence, head): merge_head_parts over parts 0..world-1,
+// the arithmetic of lse_combine_kernel (same bits as the NCCL path).
 __global__ void peer_combine_kernel(const __grid_constant__ PeerSlots src, int world, const CombineCtl ctl,
                                     void* out, int out_f16, float* lse_out, long long heads, int D,
                                     uint32_t* status) {
@@ -123,23 +124,7 @@ __global__ void peer_combine_kernel(const __grid_constant__ PeerSlots src, int w
     const long long hw = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (hw >= heads) return;
-    float M = -INFINITY;
-    for (int p = 0; p < world; ++p) M = fmaxf(M, src.lse[p][hw]);
-    float S = 0.f;
-    if (M != -INFINITY)
-        for (int p = 0; p < world; ++p) S += expf(src.lse[p][hw] - M);
-    const float lse = M == -INFINITY ? -INFINITY : M + logf(S);
-    for (int d = lane; d < D; d += 32) {
-        float acc = 0.f;
-        if (M != -INFINITY)
-            for (int p = 0; p < world; ++p) {
-                const float lp = src.lse[p][hw];
-                if (lp != -INFINITY) acc += expf(lp - lse) * src.part[p][hw * D + d];
-            }
-        if (out_f16) reinterpret_cast<__half*>(out)[hw * D + d] = __float2half_rn(acc);
-        else reinterpret_cast<float*>(out)[hw * D + d] = acc;
-    }
-    if (lse_out && lane == 0) lse_out[hw] = lse;
+    merge_head_parts(src.lse, src.part, world, hw, D, lane, out, out_f16, lse_out);
 }
 
 __global__ void peer_signal_kernel(PeerSignal sig) {

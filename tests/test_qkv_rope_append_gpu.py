@@ -36,6 +36,7 @@ SHAPES = {
     "tinyllama_b7": (2048, 32, 4, 64, 7),
     "tinyllama_b70": (2048, 32, 4, 64, 70),  # two launches of at most 64 tokens
     "llama3_8b_b16": (4096, 32, 8, 128, 16),
+    "llama3_8b_b64": (4096, 32, 8, 128, 64),  # the benchmark's shape
 }
 
 
