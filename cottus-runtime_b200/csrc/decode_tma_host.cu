@@ -104,7 +104,7 @@ CUtensorMap make_tensor_map_2d_f16(const void* base, uint64_t inner, uint64_t ou
     return map;
 }
 
-// Leading bytes of a decode workspace: the chunk queue word and one arrival
+// Leading bytes of a decode workspace: a reserved word and one arrival
 // counter per (sequence, kv head) pair, rounded to 256 bytes.
 size_t workspace_zero_prefix_bytes(int32_t batch, int32_t num_kv_heads) {
     return ((1 + (size_t)batch * (size_t)num_kv_heads) * 8 + 255) & ~size_t(255);

@@ -73,9 +73,9 @@ cudaError_t launch_decode_mma_d128(const DecodeDesc& d, cudaStream_t st);
 size_t mma_workers_d64(const DecodeDesc& d);
 size_t mma_workers_d128(const DecodeDesc& d);
 
-// Bytes at the start of a decode workspace that hold the chunk queue word
-// and the pair arrival counters (zero before a launch that has never used
-// the workspace).
+// Bytes at the start of a decode workspace that hold a reserved word and
+// the pair arrival counters (zero before a launch that has never used the
+// workspace).
 size_t workspace_zero_prefix_bytes(int32_t batch, int32_t num_kv_heads);
 
 // Generic path: any head_dim <= 512, any block size; one CTA per (seq, head).
