@@ -248,6 +248,16 @@ def start_clocks(local):
     return sampler
 
 
+def hold_gpu():
+    """Queues a ~1 ms spin on the GPU (torch's bounded sleep kernel) just
+    before a timed region, so that the host enqueues the timed steps while
+    the GPU is busy: a host stall (other processes, Python) then cannot leave
+    the GPU idle inside the region.  The region's first event is recorded
+    after the spin, so the spin is not timed."""
+    import torch
+    torch.cuda._sleep(2_000_000)
+
+
 def timed_steps(step, args, dev, world, local):
     """W untimed steps, then K steps between CUDA events on the current
     stream with the SM clocks sampled; a synchronize and a barrier (no idle
@@ -263,6 +273,7 @@ def timed_steps(step, args, dev, world, local):
         dist.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    hold_gpu()
     e0.record(stream)
     for i in range(args.steps):
         step(i)
@@ -870,6 +881,7 @@ def run_decode(args, rank, world, local):
         elapsed_ms = sum(a.elapsed_time(b) for a, b in evs)
     else:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        hold_gpu()
         e0.record(stream)
         for i in range(args.steps):
             step(args.warmup + i)
@@ -1009,6 +1021,7 @@ def device_ms(step, args, dev, world):
         dist.barrier()
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    hold_gpu()
     e0.record(stream)
     for i in range(args.steps):
         step(args.warmup + i)

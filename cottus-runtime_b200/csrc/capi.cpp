@@ -208,6 +208,19 @@ int paged_decode_signalled(const cottus_paged_decode_params* p, const PeerSignal
     const cudaError_t e = launch_peer_signal(sig, st);
     return e == cudaSuccess ? COTTUS_OK : cuda_fail(e);
 }
+
+int paged_decode_exchanged(const cottus_paged_decode_params* p, const PeerSignal& sig, const PeerMerge& pm,
+                           cudaStream_t st) {
+    int rc = validate_decode_params(p);
+    if (rc) return rc;
+    if (p->batch <= 0) return fail(COTTUS_ERR_INVALID_ARGUMENT, "empty batch");
+    DecodeDesc d = desc_from(p);
+    if (!tma_supported(d) || !mma_supported(d))
+        return fail(COTTUS_ERR_UNSUPPORTED, "the merge runs in the decode kernel only on the tensor-core path");
+    d.signal = sig;
+    d.merge = pm;
+    return run_decode(d, st);
+}
 }  // namespace cb200
 
 extern "C" {

@@ -90,7 +90,7 @@ constexpr size_t mma_smem_bytes() {
 
 // CTAs per SM the register budget is fitted to (8 or 12 warps per SM).
 #ifndef CB200_MMA_MIN_CTAS_D64
-#define CB200_MMA_MIN_CTAS_D64 2
+#define CB200_MMA_MIN_CTAS_D64 3
 #endif
 #ifndef CB200_MMA_MIN_CTAS_D128
 #define CB200_MMA_MIN_CTAS_D128 2
@@ -763,6 +763,41 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D>())
             for (int r = 0; r < a.sig.world; ++r)
                 asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.sig.flags[r] + a.sig.rank), "r"(a.sig.epoch)
                              : "memory");
+        }
+    }
+
+    // ---- split-context merge in the same launch --------------------------------
+    // Every CTA waits (bounded) until every rank's flag has reached this step
+    // (its own flag included: then every CTA of this launch has stored its
+    // partials), then merges rows CTA-strided, one warp per (sequence, head),
+    // all ranks' loads in flight together (merge_head_parts: the arithmetic of
+    // cottus_lse_combine, so the NCCL path gives the same bits).  The grid is
+    // one CTA per resident slot, so the CTAs that wait do not keep the others
+    // from running.  A serial-number comparison accepts a peer one step ahead.
+    if (a.pm.enabled) {
+        if (threadIdx.x == 0) {
+            bool ready = ld_acquire_sys(a.pm.broken_own) == 0u;
+            const long long t0 = clock64();
+            for (int r = 0; r < a.sig.world && ready; ++r)
+                while ((int32_t)(ld_acquire_sys(a.pm.flags + r) - a.sig.epoch) < 0)
+                    if (clock64() - t0 > a.pm.wait_cycles) {
+                        ready = false;
+                        break;
+                    }
+            s_last = ready;
+            if (!ready) {
+                report(a.status, COTTUS_STATUS_TIMEOUT);
+                // every later step of every rank refuses at once
+                for (int r = 0; r < a.sig.world; ++r)
+                    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(a.pm.broken[r]), "r"(1u) : "memory");
+            }
+        }
+        __syncthreads();
+        if (s_last) {
+            const long long rows = (long long)a.B * a.H;
+            for (long long hw = cid * kNW + warp; hw < rows; hw += (long long)gridDim.x * kNW)
+                merge_head_parts(a.pm.lse, a.pm.part, a.sig.world, hw, D, lane, a.pm.out, a.pm.out_f16,
+                                 a.pm.lse_out);
         }
     }
 }

@@ -65,6 +65,7 @@ struct TmaArgs {
     unsigned epoch;  // per-launch tag of the arrival counters
     float qscale;    // softmax scale * log2(e)
     PeerSignal sig;  // completion signal to the other ranks of a split context
+    PeerMerge pm;    // the split context's merge in the same launch (decode_mma_kernel)
 };
 
 // End of a warp's work.  In a split-context launch, once every warp of every
@@ -966,6 +967,7 @@ inline TmaArgs make_tma_args(const DecodeDesc& d, long long W, int G, int D) {
     a.status = d.status;
     a.epoch = next_epoch();
     a.sig = d.signal;
+    a.pm = d.merge;
     a.k_new = d.k_new;
     a.v_new = d.v_new;
     a.cos_sin = d.cos_sin;

@@ -22,6 +22,26 @@ struct PeerSignal {
     uint32_t epoch = 0;
 };
 
+// The merge of a split-context step done by the decode kernel itself, after
+// its completion signal (fast-path kernels; see peer_exchange.cu): every CTA
+// waits (bounded) until every rank's flag in `flags` has reached the signal's
+// epoch, then merges a share of the (sequence, head) rows from every rank's
+// partial slot (part / lse, peer pointers) into `out`.  A wait that runs out
+// reports COTTUS_STATUS_TIMEOUT, writes nothing and stores 1 into every
+// rank's broken word; a set broken word of this rank makes the merge refuse
+// at once.  enabled == 0: none.
+struct PeerMerge {
+    const float* part[kMaxPeers] = {};
+    const float* lse[kMaxPeers] = {};
+    uint32_t* broken[kMaxPeers] = {};
+    const uint32_t* flags = nullptr;  // this rank's flag words, one per rank
+    uint32_t* broken_own = nullptr;
+    void* out = nullptr;
+    float* lse_out = nullptr;
+    long long wait_cycles = 0;
+    int32_t out_f16 = 0, enabled = 0;
+};
+
 // One resolved decode launch.  In rope mode the context length of sequence
 // b is positions[b] + 1 and the kernel first rotates q/k and appends k/v.
 struct DecodeDesc {
@@ -49,6 +69,7 @@ struct DecodeDesc {
     void* q_out = nullptr;
     uint16_t* kv_mut = nullptr;
     PeerSignal signal;  // split-context decode across GPUs (fast path kernels)
+    PeerMerge merge;    // with signal: the merge done in the same kernel (tensor-core kernel only)
 };
 
 // Fast path: persistent stream-K TMA kernel (block_size 16, head_dim in
@@ -107,6 +128,10 @@ int validate_decode_params(const cottus_paged_decode_params* p);
 // signalled to every rank, and the stand-alone signal used after the
 // generic kernel.
 int paged_decode_signalled(const cottus_paged_decode_params* p, const PeerSignal& sig, cudaStream_t st);
+// The same step with the merge in the decode kernel itself; returns
+// COTTUS_ERR_UNSUPPORTED (nothing launched) where the shape takes another kernel.
+int paged_decode_exchanged(const cottus_paged_decode_params* p, const PeerSignal& sig, const PeerMerge& pm,
+                           cudaStream_t st);
 cudaError_t launch_peer_signal(const PeerSignal& sig, cudaStream_t st);
 
 // Host-side (cos, sin) of the reference formula (compute_primitives_cpu.cpp:54-57).

@@ -10,26 +10,29 @@
 //   1. the decode kernel writes this rank's partials into its own slot
 //      (epoch & 1) and, when its last CTA has finished, stores `epoch` into
 //      flag[rank] of every rank's buffer (decode_tma.cuh: signal_done);
-//   2. the combine kernel waits (bounded) until every rank's flag in its own
-//      buffer has reached `epoch`, then reads every rank's slot directly
-//      (peer loads) and merges them, the arithmetic of cottus_lse_combine.
+//   2. every rank waits (bounded) until every rank's flag in its own buffer
+//      has reached `epoch`, then reads every rank's slot directly (peer
+//      loads) and merges them, the arithmetic of cottus_lse_combine: on the
+//      tensor-core path in the decode kernel itself, its CTAs taking the
+//      rows in turn (decode_mma.cuh), otherwise in a combine kernel.
 // Two slots suffice: a rank overwrites slot s at step n+2 only after its
-// combine of step n+1, which waited for every rank's step-n+1 decode, which
-// each rank started after its own combine of step n had read slot s.  The
-// same chain bounds how far a peer can run ahead: when this rank's combine
-// of step n polls, a peer's flag reads n or n+1 (the peer may already have
+// merge of step n+1, which waited for every rank's step-n+1 decode, which
+// each rank started after its own merge of step n had read slot s.  The
+// same chain bounds how far a peer can run ahead: when this rank's merge of
+// step n polls, a peer's flag reads n or n+1 (the peer may already have
 // finished its decode of step n+1), never more, so the wait accepts any
 // flag at or past `epoch` (serial-number comparison, wrap-safe).
 //
-// Failure handling: a combine whose wait runs out reports
+// Failure handling: a merge whose wait runs out reports
 // COTTUS_STATUS_TIMEOUT, writes nothing, and sets the broken word in its own
-// buffer and in every peer's; from then on every combine of every rank of
+// buffer and in every peer's; from then on every merge of every rank of
 // this exchange reports COTTUS_STATUS_TIMEOUT at once without waiting or
 // writing, until the ranks destroy the exchange and create a new one (the
 // epochs of the ranks may disagree after a missed step, so no later step of
-// the old exchange can be trusted).  The combine also returns the decode's
-// CTA counter to zero, which a decode warp that gave up on a wait leaves
-// behind.
+// the old exchange can be trusted).  The combine kernel also returns the
+// decode's CTA counter to zero, which a decode warp that gave up on a wait
+// leaves behind (the decode kernel that merges itself resets it when it
+// completes normally; after a wait that gave up, the exchange is broken).
 // Plain loads and stores only (no bulk or tensor copies of peer memory).
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
@@ -49,6 +52,18 @@ namespace {
 
 constexpr size_t kAlign = 256;
 constexpr long long kPeerWaitCycles = 2000000000LL;  // default wait limit: about a second at 2 GHz
+}  // namespace
+}  // namespace cb200
+
+// The merge of a step runs in the decode kernel itself where the shape takes
+// the tensor-core kernel (one launch per step); 0 keeps the decode + combine
+// kernel pair for every shape.
+#ifndef CB200_SPLIT_MERGE_IN_DECODE
+#define CB200_SPLIT_MERGE_IN_DECODE 1
+#endif
+
+namespace cb200 {
+namespace {
 
 size_t align_up(size_t x) { return (x + kAlign - 1) & ~(kAlign - 1); }
 
@@ -84,12 +99,6 @@ struct CombineCtl {
     uint32_t epoch;
     long long wait_cycles;
 };
-
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 
 // One warp per (sequence, head): merge_head_parts over parts 0..world-1,
 // the arithmetic of lse_combine_kernel (same bits as the NCCL path).
@@ -285,6 +294,25 @@ int cottus_split_decode(const cottus_paged_decode_params* p, cottus_peer_exchang
     sig.rank = ex->rank;
     sig.world = ex->world;
     sig.epoch = epoch;
+#if CB200_SPLIT_MERGE_IN_DECODE
+    // on the tensor-core path the decode kernel merges the ranks' partials itself
+    cb200::PeerMerge pm;
+    for (int r = 0; r < ex->world; ++r) {
+        pm.part[r] = reinterpret_cast<const float*>(ex->base[r] + slot);
+        pm.lse[r] = reinterpret_cast<const float*>(ex->base[r] + slot + ex->lay.part_bytes);
+        pm.broken[r] = reinterpret_cast<uint32_t*>(ex->base[r] + ex->lay.broken);
+    }
+    pm.flags = reinterpret_cast<const uint32_t*>(ex->local + ex->lay.flags);
+    pm.broken_own = reinterpret_cast<uint32_t*>(ex->local + ex->lay.broken);
+    pm.out = p->out;
+    pm.out_f16 = p->out_dtype == COTTUS_F16;
+    pm.lse_out = p->lse_out;
+    pm.wait_cycles = ex->wait_cycles;
+    pm.enabled = 1;
+    const int rcx = cb200::paged_decode_exchanged(&q, sig, pm, reinterpret_cast<cudaStream_t>(stream));
+    if (rcx != COTTUS_ERR_UNSUPPORTED) return rcx;
+#endif
+    // otherwise: the decode (its completion signalled), then a combine kernel
     const int rc = cb200::paged_decode_signalled(&q, sig, reinterpret_cast<cudaStream_t>(stream));
     if (rc != COTTUS_OK) return rc;
     // 2. wait for every rank's flag, pull and merge

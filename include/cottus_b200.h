@@ -378,11 +378,15 @@ int cottus_decode_batch_sequence(const cottus_decode_batch *b, int64_t seq_id, i
  * lockstep with the other ranks: p describes this rank's page range of
  * every sequence (its pool shard, block table and token counts); p->out
  * receives the merged output [batch][num_heads][head_dim] and p->lse_out
- * (optional) the merged natural-log LSE.  One decode kernel (partials into
- * this rank's exchange buffer, completion flagged to every rank by its last
- * CTA) and one combine kernel (bounded wait until every rank has flagged
- * this step or a later one, then peer loads over NVLink and the merge of
- * cottus_lse_combine).  At most 8 ranks.
+ * (optional) the merged natural-log LSE.  One decode kernel writes this
+ * rank's partials into its exchange buffer and, once all its CTAs have
+ * stored them, flags completion to every rank; then (bounded) waits until
+ * every rank has flagged this step or a later one, and merges the ranks'
+ * partials with peer loads over NVLink (the arithmetic of
+ * cottus_lse_combine).  On the tensor-core decode path (grouped queries,
+ * head_dim 64/128, block size 16) the wait and merge run in the decode
+ * kernel itself; other shapes use a separate combine kernel.  At most 8
+ * ranks.
  *
  * Failure detection: a rank that does not take part in a step makes the
  * others' combine give up after the wait limit (default 2e9 GPU clock
