@@ -201,6 +201,14 @@ __device__ __forceinline__ void grid_dependents_launch() { asm volatile("griddep
 // Device-scope acquire-release fence: orders this thread's earlier memory
 // operations before its later ones as seen by other SMs.
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// A plain global load issued where it stands (volatile asm: the compiler does
+// not sink it into a later branch that uses it), so that it is in flight
+// together with the loads issued next to it.
+__device__ __forceinline__ int ld_now_i32(const int32_t* p) {
+    int v;
+    asm volatile("ld.global.b32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
 // Relaxed device-scope load (reads the current value at the coherence point).
 __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
     unsigned long long v;

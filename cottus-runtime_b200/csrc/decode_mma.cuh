@@ -112,6 +112,18 @@ template <int D>
 constexpr int pair_pad() { return D == 64 ? CB200_PAIR_PAD_D64 : CB200_PAIR_PAD_D128; }
 // Fewest units in a CTA's chunk (4 per warp).
 constexpr long long kMinChunkCta = 4 * kNW;
+// Own units per warp warmed in L2 before the wait for the preceding kernel.
+#ifndef CB200_MMA_WARM_PAGES
+#define CB200_MMA_WARM_PAGES 3
+#endif
+// Whether a vote on the lanes' own scores gates the reduction of a page's max
+// (measured: faster at head_dim 64 and at head_dim 128 with groups of 4; at
+// head_dim 128 with groups of 8 the long-context shape ran 0.7 % slower).
+#ifndef CB200_MMA_VOTE_D128_G8
+#define CB200_MMA_VOTE_D128_G8 0
+#endif
+template <int D, int G>
+constexpr bool vote_max() { return D == 128 && G == 8 ? CB200_MMA_VOTE_D128_G8 : true; }
 
 // One segment of a chunk [u0, u1): the chunk's real units inside one
 // (sequence, kv head) pair.  c is at the segment's first page, r0 counts
@@ -144,6 +156,44 @@ __device__ __forceinline__ void cursor_advance(Cursor& c, const TmaArgs& a, int 
         return;
     }
     for (int i = 0; i < n; ++i) cursor_next<ROPE>(c, a, PAD);
+}
+
+// A warp's first own units (units warp, warp + kNW, ... of its chunk): lane
+// j <= RING gets own unit j's block-table index and kv head (idx -1: no such
+// unit); count is the number of own units among the first RING.  With REGS
+// the walk reads nothing but the snapshot r, so that the result computed
+// before the wait for the preceding kernel is the one computed after it
+// whenever the lengths read again match the snapshot; without, it reads the
+// lengths (batches above kPlanRegs * 32 sequences, after the wait).
+struct PrimeIdx {
+    long long idx;
+    int h, count;
+};
+template <int RING, bool REGS, bool ROPE, int PAD>
+__device__ __forceinline__ PrimeIdx prime_index(const WorkerPlan& pl, const PlanRegs& r, const TmaArgs& a, int warp,
+                                                int lane) {
+    PrimeIdx x = {-1, 0, 0};
+    if (pl.u0 >= pl.u1) return x;
+    Cursor c = pl.cur;
+    int step = warp;
+    for (int j = 0; j <= RING; ++j) {
+        if (c.p + step < c.np) {
+            c.p += step;
+        } else {
+            for (int i = 0; i < step; ++i) {
+                if constexpr (REGS) cursor_next_regs(c, r, a, lane, PAD);
+                else cursor_next<ROPE>(c, a, PAD);
+            }
+        }
+        if (c.b >= a.B || c.ps + c.p >= pl.u1) break;
+        if (lane == j) {
+            x.idx = (long long)c.b * a.maxb + c.p;
+            x.h = c.h;
+        }
+        if (j < RING) ++x.count;
+        step = kNW;
+    }
+    return x;
 }
 
 // The new token of a pair (fused step), lane < D/8 of the warp that owns the
@@ -214,22 +264,31 @@ __device__ __noinline__ void arrive_cut_pair(const MergeArgs a, long long chunk,
                                            unsigned long long hint, int* s_last) {
     const long long w0 = pps / chunk, w1 = (pps + pnp - 1) / chunk;
     const int nparts = (int)(w1 - w0 + 1);
-    fence_acq_rel_gpu();  // this thread's partial stores are visible device-wide before the arrival
-    __syncthreads();
+    __syncthreads();  // every thread's partial stores, then one release fence for the CTA
     if (threadIdx.x == 0) {
+        fence_acq_rel_gpu();
         unsigned long long* ctr = a.counters + 1 + (long long)pb * a.Hkv + ph;
         unsigned long long old = hint;
         int last = 0;
-        while (true) {  // a failed attempt means another part arrived: at most nparts rounds
-            const unsigned long long nv =
-                (unsigned)(old >> 32) == a.epoch ? old + 1 : (((unsigned long long)a.epoch << 32) | 1ull);
-            const bool fin = (int)(nv & 0xffffffffull) == nparts;
-            const unsigned long long prev = atomicCAS(ctr, old, fin ? 0ull : nv);
+        // Once a part of this launch has arrived, the counter carries this
+        // launch's tag until the pair completes (which needs this part): an
+        // add.  Before that, the first arrival replaces whatever the word holds
+        // by (tag, 1) with a compare-and-swap; one that fails because another
+        // part arrived in between falls back to the add.
+        bool added = false;
+        while ((unsigned)(old >> 32) != a.epoch) {
+            const unsigned long long first = ((unsigned long long)a.epoch << 32) | 1ull;
+            const unsigned long long prev = atomicCAS(ctr, old, first);
             if (prev == old) {
-                last = fin;
+                added = true;
                 break;
             }
             old = prev;
+        }
+        if (!added) {
+            old = atomicAdd(ctr, 1ull);
+            last = (int)(old & 0xffffffffull) + 1 == nparts;
+            if (last) *reinterpret_cast<volatile unsigned long long*>(ctr) = 0ull;  // every part is in: no other writer
         }
         *s_last = last;
     }
@@ -318,46 +377,6 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D>())
     __syncthreads();
 
     const long long W = gridDim.x, cid = blockIdx.x;
-    // The plan is made before the wait for the preceding kernel, from a
-    // snapshot of the lengths that kernel may still be writing, and the warp's
-    // first pages are warmed in L2 from it (TMA prefetch: nothing written;
-    // block ids range-checked, the tensor map bounds the box; L2 is the point
-    // of coherence, so a stale snapshot only warms the wrong lines).  After
-    // the wait the lengths are read again: the plan is kept if they match,
-    // else made again.  Batches above kPlanRegs * 32 sequences plan after the
-    // wait only.
-    const bool small = a.B <= 32 * kPlanRegs;
-    PlanRegs snap;
-    WorkerPlan pl;
-    if (small) {
-        snap = load_plan_regs<ROPE>(a, lane);
-        pl = plan_from_regs<ROPE>(a, snap, cid, W, lane, kMinChunkCta, PAD);
-        if (pl.u0 < pl.u1 && pages_before(pl.cur, a, pl.u1) > 0) {
-            Cursor wc = pl.cur;
-            cursor_advance<ROPE, PAD>(wc, a, warp);
-            for (int i = 0; i < kWarmPages && wc.b < a.B && wc.ps + wc.p < pl.u1; ++i) {
-                if (lane == 0 && wc.p < a.maxb) {
-                    const int blk = a.bt[(long long)wc.b * a.maxb + wc.p];
-                    if (blk >= 0 && (long long)blk < a.num_blocks)
-                        for (int q = 0; q < REG; ++q)
-                            tma_prefetch_l2_3d(&kv_map, q * 64, wc.h, (blk * a.L + a.layer) * (2 * kBS));
-                }
-                cursor_advance<ROPE, PAD>(wc, a, kNW);
-            }
-        }
-    }
-    grid_dependency_wait();
-    grid_dependents_launch();
-    if (small) {
-        const PlanRegs now = load_plan_regs<ROPE>(a, lane);
-        if (!same_plan_regs<ROPE>(snap, now)) pl = plan_from_regs<ROPE>(a, now, cid, W, lane, kMinChunkCta, PAD);
-        if (warp == 0) zero_fill_from_regs<D, ROPE>(a, now, cid, lane);
-    } else {
-        pl = plan_worker<D, ROPE>(a, cid, W, lane, kMinChunkCta, warp == 0, PAD);
-    }
-    const long long chunk = pl.chunk, u0 = pl.u0, u1 = pl.u1;
-    const bool has_work = u0 < u1 && pages_before(pl.cur, a, u1) > 0;
-
     // fragment coordinates of this lane
     const int qc = lane & 3;   // column pair: heads 2qc, 2qc+1 of C fragments
     const int qr = lane >> 2;  // row: token qr / qr+8 of C fragments; head qr of B fragments
@@ -409,6 +428,56 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D>())
         }
     };
 
+    // The plan is made before the wait for the preceding kernel, from a
+    // snapshot of the lengths that kernel may still be writing, with the
+    // block-table entries of the warp's first units, and those pages are
+    // warmed in L2 (TMA prefetch: nothing written; block ids range-checked,
+    // the tensor map bounds the box; L2 is the point of coherence, so a stale
+    // snapshot only warms the wrong lines).  These early reads go to L2
+    // (ld.global.cg) and leave nothing in L1.  After the wait the lengths and
+    // the table entries are read again in one round: plan and entries are
+    // kept if the lengths match the snapshot (both were computed from it
+    // alone), else made again.  Batches above kPlanRegs * 32 sequences plan
+    // after the wait only.
+    const bool small = a.B <= 32 * kPlanRegs;
+    PlanRegs snap;
+    WorkerPlan pl;
+    PrimeIdx pi;
+    int prime_blk = 0;  // lane j <= RING: block id of own unit j
+    if (small) {
+        snap = load_plan_regs<ROPE, true>(a, lane);
+        pl = plan_from_regs<ROPE>(a, snap, cid, W, lane, kMinChunkCta, PAD);
+        pi = prime_index<RING, true, ROPE, PAD>(pl, snap, a, warp, lane);
+        if (lane < CB200_MMA_WARM_PAGES && lane < pi.count) {
+            const int blk = __ldcg(a.bt + pi.idx);
+            if (blk >= 0 && (long long)blk < a.num_blocks)
+                for (int q = 0; q < REG; ++q)
+                    tma_prefetch_l2_3d(&kv_map, q * 64, pi.h, (blk * a.L + a.layer) * (2 * kBS));
+        }
+    }
+    grid_dependency_wait();
+    grid_dependents_launch();
+    // (the first segment's query is loaded in the same round, from the same plan)
+    if (small) {
+        const PlanRegs now = load_plan_regs<ROPE>(a, lane);
+        prime_blk = pi.idx >= 0 ? ld_now_i32(a.bt + pi.idx) : 0;
+        if (pl.u0 < pl.u1 && pages_before(pl.cur, a, pl.u1) > 0) load_q(pl.cur.b, pl.cur.h, pl.cur.n);
+        if (!same_plan_regs<ROPE>(snap, now)) {
+            pl = plan_from_regs<ROPE>(a, now, cid, W, lane, kMinChunkCta, PAD);
+            pi = prime_index<RING, true, ROPE, PAD>(pl, now, a, warp, lane);
+            prime_blk = pi.idx >= 0 ? a.bt[pi.idx] : 0;
+            if (pl.u0 < pl.u1 && pages_before(pl.cur, a, pl.u1) > 0) load_q(pl.cur.b, pl.cur.h, pl.cur.n);
+        }
+        if (warp == 0) zero_fill_from_regs<D, ROPE>(a, now, cid, lane);
+    } else {
+        pl = plan_worker<D, ROPE>(a, cid, W, lane, kMinChunkCta, warp == 0, PAD);
+        pi = prime_index<RING, false, ROPE, PAD>(pl, snap, a, warp, lane);
+        prime_blk = pi.idx >= 0 ? a.bt[pi.idx] : 0;
+        if (pl.u0 < pl.u1 && pages_before(pl.cur, a, pl.u1) > 0) load_q(pl.cur.b, pl.cur.h, pl.cur.n);
+    }
+    const long long chunk = pl.chunk, u0 = pl.u0, u1 = pl.u1;
+    const bool has_work = u0 < u1 && pages_before(pl.cur, a, u1) > 0;
+
     // ---- this warp's units: the chunk's real units warp, warp + 4, ... -------
     auto valid = [&](const Cursor& c) { return c.b < a.B && c.ps + c.p < u1; };
     int issued = 0, mine = 0;
@@ -451,33 +520,21 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D>())
     };
 
     if (has_work) {
-        // prime the ring: the block ids of the first RING own units are loaded by
-        // RING lanes at once, then lane 0 issues the loads back to back
+        // prime the ring: lane 0 issues the loads of the first own units back to
+        // back, with the block ids read with the plan
         cursor_advance<ROPE, PAD>(ic, a, warp);
         ic_ok = valid(ic);
-        int prime = 0, my_blk = 0;
-        {
-            Cursor pc = ic;
-            bool pc_ok = ic_ok;
-            while (pc_ok && prime < RING) {
-                if (lane == prime) my_blk = a.bt[(long long)pc.b * a.maxb + pc.p];
-                ++prime;
-                cursor_advance<ROPE, PAD>(pc, a, kNW);
-                pc_ok = valid(pc);
-            }
-        }
-        for (int j = 0; j < prime; ++j) {
-            blk_next = __shfl_sync(FULL, my_blk, j);
+        for (int j = 0; j < pi.count; ++j) {
+            blk_next = __shfl_sync(FULL, prime_blk, j);
             issue_one(false);
         }
-        if (ic_ok && lane == 0) blk_next = a.bt[(long long)ic.b * a.maxb + ic.p];
+        if (ic_ok) blk_next = __shfl_sync(FULL, prime_blk, pi.count);
     }
 
     Segment seg;
     seg.c = pl.cur;
     seg.r0 = 0;
     seg.len = has_work ? pages_before(pl.cur, a, u1) : 0;
-    if (has_work) load_q(seg.c.b, seg.c.h, seg.c.n);
 
     bool ok = true;  // this warp's waits all completed
     while (seg.len > 0) {
@@ -602,30 +659,36 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D>())
             const bool ok0 = qr < n_valid, ok1 = qr + 8 < n_valid;
             const float s00 = ok0 ? s[0] * a.qscale : -INFINITY, s01 = ok0 ? s[1] * a.qscale : -INFINITY;
             const float s10 = ok1 ? s[2] * a.qscale : -INFINITY, s11 = ok1 ? s[3] * a.qscale : -INFINITY;
+            // The running max is raised only when the page's max exceeds it by
+            // more than 8; one vote on the lanes' own scores decides whether the
+            // page's max is needed at all (the same decisions as reducing it on
+            // every page, without the 3 dependent shuffles on most pages).
             float c0 = fmaxf(s00, s10), c1 = fmaxf(s01, s11);
+            if (!vote_max<D, G>() || __any_sync(FULL, c0 > m0 + 8.0f || c1 > m1 + 8.0f)) {
 #pragma unroll
-            for (int sh = 4; sh < 32; sh <<= 1) {
-                c0 = fmaxf(c0, __shfl_xor_sync(FULL, c0, sh));
-                c1 = fmaxf(c1, __shfl_xor_sync(FULL, c1, sh));
-            }
-            if (c0 > m0 + 8.0f) {
-                const float al = exp2f(m0 - c0);
-                m0 = c0;
-                l0 *= al;
-#pragma unroll
-                for (int j = 0; j < KS; ++j) {
-                    o[j][0] *= al;
-                    o[j][2] *= al;
+                for (int sh = 4; sh < 32; sh <<= 1) {
+                    c0 = fmaxf(c0, __shfl_xor_sync(FULL, c0, sh));
+                    c1 = fmaxf(c1, __shfl_xor_sync(FULL, c1, sh));
                 }
-            }
-            if (c1 > m1 + 8.0f) {
-                const float al = exp2f(m1 - c1);
-                m1 = c1;
-                l1 *= al;
+                if (c0 > m0 + 8.0f) {
+                    const float al = exp2f(m0 - c0);
+                    m0 = c0;
+                    l0 *= al;
 #pragma unroll
-                for (int j = 0; j < KS; ++j) {
-                    o[j][1] *= al;
-                    o[j][3] *= al;
+                    for (int j = 0; j < KS; ++j) {
+                        o[j][0] *= al;
+                        o[j][2] *= al;
+                    }
+                }
+                if (c1 > m1 + 8.0f) {
+                    const float al = exp2f(m1 - c1);
+                    m1 = c1;
+                    l1 *= al;
+#pragma unroll
+                    for (int j = 0; j < KS; ++j) {
+                        o[j][1] *= al;
+                        o[j][3] *= al;
+                    }
                 }
             }
             const float p00 = ok0 ? exp2f(s00 - m0) : 0.f, p01 = ok0 ? exp2f(s01 - m1) : 0.f;

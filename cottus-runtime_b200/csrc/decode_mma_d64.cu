@@ -1,8 +1,8 @@
-// Tensor-core path instantiations for head_dim 64 (ring of 4 pages per warp).
+// Tensor-core path instantiations for head_dim 64 (ring of 3 pages per warp).
 #include "decode_mma.cuh"
 
 #ifndef CB200_MMA_RING_D64
-#define CB200_MMA_RING_D64 4
+#define CB200_MMA_RING_D64 3
 #endif
 
 namespace cb200 {

@@ -95,16 +95,18 @@ __device__ __forceinline__ void signal_done(const TmaArgs& a, int lane, unsigned
 }
 
 // Pages of sequence b, or 0 when its context is empty or invalid; *ctx_out
-// receives the context length.
-template <bool ROPE>
+// receives the context length.  CG: read at L2 (ld.global.cg), for reads made
+// before the wait for the preceding kernel, so that no line of lengths that
+// kernel may still write is left in L1.
+template <bool ROPE, bool CG = false>
 __device__ __forceinline__ int seq_pages(const TmaArgs& a, int b, int* ctx_out = nullptr) {
     int n;
     if (ROPE) {
-        int pos = a.positions[b];
+        const int pos = CG ? __ldcg(a.positions + b) : a.positions[b];
         if (pos < 0 || pos >= a.max_pos) return 0;
         n = pos + 1;
     } else {
-        n = a.ctx[b];
+        n = CG ? __ldcg(a.ctx + b) : a.ctx[b];
     }
     if (ctx_out) *ctx_out = n;
     if (n <= 0 || n > a.maxb * kBS) return 0;
@@ -308,17 +310,52 @@ __device__ __forceinline__ CachedHit locate_cached(const int (&pg)[kPlanRegs], l
 struct PlanRegs {
     int pg[kPlanRegs], cx[kPlanRegs];
 };
-template <bool ROPE>
+template <bool ROPE, bool CG = false>
 __device__ __forceinline__ PlanRegs load_plan_regs(const TmaArgs& a, int lane) {
     PlanRegs r;
 #pragma unroll
     for (int i = 0; i < kPlanRegs; ++i) {
         const int b = lane + 32 * i;
         r.cx[i] = 0;
-        r.pg[i] = b < a.B ? seq_pages<ROPE>(a, b, &r.cx[i]) : 0;
+        r.pg[i] = b < a.B ? seq_pages<ROPE, CG>(a, b, &r.cx[i]) : 0;
     }
     return r;
 }
+// cursor_next over a snapshot (no memory reads): the same steps, with the
+// page counts and lengths of later sequences taken from the lanes that hold
+// them.  A plan made before the wait for the preceding kernel from one
+// snapshot is then exactly the plan made after it when the lengths read
+// again match the snapshot.
+__device__ __forceinline__ void cursor_next_regs(Cursor& c, const PlanRegs& r, const TmaArgs& a, int lane, int pad) {
+    constexpr unsigned FULL = 0xffffffffu;
+    if (++c.p < c.np) return;
+    c.ps += c.np + pad;
+    c.p = 0;
+    if (++c.h < a.Hkv) return;
+    c.h = 0;
+    int reg = -1, src = 0;  // the first sequence after c.b with pages: register slot and lane
+#pragma unroll
+    for (int i = 0; i < kPlanRegs; ++i) {
+        const unsigned hit = __ballot_sync(FULL, 32 * i + lane > c.b && r.pg[i] > 0);
+        if (reg < 0 && hit) {
+            reg = i;
+            src = __ffs(hit) - 1;
+        }
+    }
+    int np = 1, n = 0;
+#pragma unroll
+    for (int i = 0; i < kPlanRegs; ++i) {  // register arrays are indexed with constants only
+        const int np_i = __shfl_sync(FULL, r.pg[i], src), n_i = __shfl_sync(FULL, r.cx[i], src);
+        if (i == reg) {
+            np = np_i;
+            n = n_i;
+        }
+    }
+    c.b = reg < 0 ? a.B : 32 * reg + src;
+    c.np = np;
+    c.n = n;
+}
+
 template <bool ROPE>
 __device__ __forceinline__ bool same_plan_regs(const PlanRegs& x, const PlanRegs& y) {
     bool same = true;
@@ -355,8 +392,7 @@ __device__ __forceinline__ void zero_fill_from_regs(const TmaArgs& a, const Plan
     }
 }
 
-// The plan of worker w from a snapshot (reads only: the lengths of the
-// sequences after the first one, when the chunk starts in a virtual unit).
+// The plan of worker w from a snapshot (no memory reads).
 template <bool ROPE>
 __device__ __forceinline__ WorkerPlan plan_from_regs(const TmaArgs& a, const PlanRegs& r, long long w,
                                                      long long W, int lane, long long min_chunk, int pad) {
@@ -392,7 +428,7 @@ __device__ __forceinline__ WorkerPlan plan_from_regs(const TmaArgs& a, const Pla
     pl.cur.ps = hit.excl + (long long)pl.cur.h * (fnp + pad);
     if (pl.cur.p >= fnp) {  // a virtual unit: the next real one is page 0 of the next pair
         pl.cur.p = fnp - 1;
-        cursor_next<ROPE>(pl.cur, a, pad);
+        cursor_next_regs(pl.cur, r, a, lane, pad);
     }
     return pl;
 }
@@ -454,7 +490,7 @@ __device__ __forceinline__ void warm_first_pages(const TmaArgs& a, const CUtenso
 #pragma unroll
     for (int i = 0; i < kPlanRegs; ++i) {
         const int b = lane + 32 * i;
-        pg[i] = b < a.B ? seq_pages<ROPE>(a, b) : 0;
+        pg[i] = b < a.B ? seq_pages<ROPE, true>(a, b) : 0;
         total += pg[i] > 0 ? pg[i] + pad : 0;
     }
 #pragma unroll
@@ -477,7 +513,7 @@ __device__ __forceinline__ void warm_first_pages(const TmaArgs& a, const CUtenso
         const long long r = u - hit.excl;
         const int h = (int)(r / (np + pad)), p = (int)(r % (np + pad));
         if (h >= a.Hkv || p >= np || p >= a.maxb) continue;  // past the table, or a virtual unit
-        const int blk = a.bt[(long long)hit.b * a.maxb + p];
+        const int blk = __ldcg(a.bt + (long long)hit.b * a.maxb + p);
         if (blk >= 0 && (long long)blk < a.num_blocks)
             for (int q = 0; q < boxes; ++q) tma_prefetch_l2_3d(map, q * box_elems, h, (blk * a.L + a.layer) * (2 * kBS));
     }
