@@ -834,7 +834,9 @@ def run_decode(args, rank, world, local):
         from cottus_b200 import parallel
         if args.exchange == "peer":
             exchange = parallel.PeerExchange(w.B, w.H, w.D)
-    launches_per_step = 2 if split else 1
+    # split over ranks: through peer memory the tensor-core decode kernel also merges the ranks' partials
+    # (one launch); through NCCL a decode and an LSE combine launch around the all-gathers
+    launches_per_step = (1 if args.exchange == "peer" else 2) if split else 1
 
     def step(i):
         layer = i % w.L
@@ -996,8 +998,9 @@ def run_decode(args, rank, world, local):
         "pct_hbm_peak": value / world / peak * 100,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "peak_kind": peak_kind,
-                     "kernel": decode_kernel_name(w) + ((" + peer_combine_kernel" if args.exchange == "peer"
-                                                        else " + lse_combine_kernel") if split else "") +
+                     "kernel": decode_kernel_name(w) +
+                     ((" with the peer merge in the same launch" if args.exchange == "peer"
+                       else " + lse_combine_kernel") if split else "") +
                      ": one decode launch per step",
                      "kernel_ms": kern_ms, "kernel_ms_alone": k_ms, "algorithmic_bytes": alg},
         "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": clocks,
@@ -1134,7 +1137,7 @@ def split_kv_extra(args, rank, world, local):
                 "GB_s": gb, "frac_of_n_peaks": gb / (world * peak), "ms_per_step_nccl": ms_nccl,
                 "ms_decode_alone": ms_dec, "exchange_and_merge_ms": ms_peer - ms_dec, "ms_per_step_1gpu": ms1,
                 "efficiency_vs_1gpu": (ms1 / (world * ms_peer)) if ms1 else None,
-                "gpu_launches": 2 * args.steps})
+                "gpu_launches": args.steps})
     return res
 
 

@@ -123,8 +123,10 @@ class PeerExchange:
 def split_kv_decode_peer(query, kv_pool, block_table, context_lens, exchange: PeerExchange, *, num_kv_heads,
                          head_dim, block_size, num_layers=1, layer=0, num_physical_blocks=None,
                          out_dtype=torch.float16, out=None, lse_out=None, status=None, stream=None):
-    """split_kv_decode with the exchange through peer memory: one decode
-    kernel and one combine kernel per rank, no collective call."""
+    """split_kv_decode with the exchange through peer memory, no collective
+    call: on the tensor-core path (grouped queries) one decode kernel per
+    rank that also merges every rank's partials; otherwise a decode kernel
+    and a combine kernel per rank."""
     B, H, D = query.shape
     if out is None:
         out = torch.empty((B, H, D), dtype=out_dtype, device=query.device)

@@ -115,9 +115,11 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
     // tile read neighbouring 128-byte pieces of the same weight rows
     const int nsteps = split < a.ksteps ? (a.ksteps - split + a.splits - 1) / a.splits : 0;
     const int npre = nsteps < kQStages ? nsteps : kQStages;
-    // (the finish kernel is released at exit: released at the start, with
-    // the finish kernels also releasing early, a chained decode step
-    // measured up to 28 us slower)
+    // (the finish kernel is released once this CTA's multiplies are done;
+    // released at the start, with the finish kernels also releasing early, a
+    // chained decode step measured up to 28 us slower; released at exit,
+    // the O-projection took 12.6 us instead of 12.0 and the QKV step 17.9
+    // instead of 17.2)
 
     if (threadIdx.x == 0) {
         prefetch_tensormap(&wmap);
@@ -205,6 +207,9 @@ __global__ void __launch_bounds__(kQThreads) qkv_proj_kernel(const __grid_consta
     const bool got = mbar_wait_bounded(done, 0);
     tc_fence_after();
     const bool ok = __syncthreads_and(got) && !failed;
+    // the finish kernel may become resident now; it waits for this grid
+    // (grid_dependency_wait) before it reads a partial
+    grid_dependents_launch();
     if (!ok && threadIdx.x == 0) {
         // report, let the copies still in flight land (bounded), and go on
         // with zero partials
