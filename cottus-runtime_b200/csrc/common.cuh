@@ -237,12 +237,38 @@ __device__ __forceinline__ int32_t div_up(int32_t a, int32_t b) { return (a + b 
 // round trip even when the parts live in other GPUs' memory); a lane covers
 // 4 consecutive dims.
 constexpr int kMergeParts = 8;
+// Dims d .. d+3 (fewer at the end of the row) of every part's row.
+__device__ __forceinline__ void load_part_rows(float4 (&x)[kMergeParts], const float* const (&row)[kMergeParts], int P,
+                                               long long hw, int D, int d) {
+    const int n = D - d < 4 ? D - d : 4;
+#pragma unroll
+    for (int p = 0; p < kMergeParts; ++p) {
+        x[p] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (p < P) {
+            const float* src = row[p] + hw * D + d;
+            if (n == 4 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+                x[p] = __ldcg(reinterpret_cast<const float4*>(src));
+            } else {
+                x[p].x = __ldcg(src);
+                if (n > 1) x[p].y = __ldcg(src + 1);
+                if (n > 2) x[p].z = __ldcg(src + 2);
+                if (n > 3) x[p].w = __ldcg(src + 3);
+            }
+        }
+    }
+}
 __device__ __forceinline__ void merge_head_parts(const float* const (&lse)[kMergeParts],
                                                  const float* const (&row)[kMergeParts], int P, long long hw, int D,
                                                  int lane, void* out, int out_f16, float* lse_out) {
     float lp[kMergeParts];
 #pragma unroll
     for (int p = 0; p < kMergeParts; ++p) lp[p] = p < P ? __ldcg(lse[p] + hw) : -INFINITY;
+    // the lane's first dims of every part are requested together with the
+    // LSEs (their addresses do not depend on them): one round trip, not two;
+    // a part without valid tokens (LSE -inf) is loaded but never added
+    const int d0 = lane * 4;
+    float4 x0[kMergeParts];
+    if (d0 < D) load_part_rows(x0, row, P, hw, D, d0);
     float M = -INFINITY;
 #pragma unroll
     for (int p = 0; p < kMergeParts; ++p) M = fmaxf(M, lp[p]);
@@ -256,24 +282,15 @@ __device__ __forceinline__ void merge_head_parts(const float* const (&lse)[kMerg
     float wt[kMergeParts];
 #pragma unroll
     for (int p = 0; p < kMergeParts; ++p) wt[p] = (p < P && lp[p] != -INFINITY) ? expf(lp[p] - L) : 0.f;
-    for (int d = lane * 4; d < D; d += 128) {
+    for (int d = d0; d < D; d += 128) {
         float4 x[kMergeParts];
-        const int n = D - d < 4 ? D - d : 4;
+        if (d == d0) {
 #pragma unroll
-        for (int p = 0; p < kMergeParts; ++p) {
-            x[p] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (p < P && lp[p] != -INFINITY) {
-                const float* src = row[p] + hw * D + d;
-                if (n == 4 && (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
-                    x[p] = __ldcg(reinterpret_cast<const float4*>(src));
-                } else {
-                    x[p].x = __ldcg(src);
-                    if (n > 1) x[p].y = __ldcg(src + 1);
-                    if (n > 2) x[p].z = __ldcg(src + 2);
-                    if (n > 3) x[p].w = __ldcg(src + 3);
-                }
-            }
+            for (int p = 0; p < kMergeParts; ++p) x[p] = x0[p];
+        } else {
+            load_part_rows(x, row, P, hw, D, d);
         }
+        const int n = D - d < 4 ? D - d : 4;
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int p = 0; p < kMergeParts; ++p) {

@@ -837,7 +837,13 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D>())
     // cottus_lse_combine, so the NCCL path gives the same bits).  The grid is
     // one CTA per resident slot, so the CTAs that wait do not keep the others
     // from running.  A serial-number comparison accepts a peer one step ahead.
+    // Only the CTAs that have rows to merge (one row per warp) wait; the
+    // others leave at once, so that the next launch's CTAs can take their
+    // slots and run their prologue during the exchange.
     if (a.pm.enabled) {
+        const long long rows = (long long)a.B * a.H;
+        const long long mctas = min((long long)gridDim.x, (rows + kNW - 1) / kNW);
+        if (cid >= mctas) return;
         if (threadIdx.x == 0) {
             bool ready = ld_acquire_sys(a.pm.broken_own) == 0u;
             const long long t0 = clock64();
@@ -857,8 +863,7 @@ __global__ void __launch_bounds__(kNW * 32, mma_min_ctas<D>())
         }
         __syncthreads();
         if (s_last) {
-            const long long rows = (long long)a.B * a.H;
-            for (long long hw = cid * kNW + warp; hw < rows; hw += (long long)gridDim.x * kNW)
+            for (long long hw = cid * kNW + warp; hw < rows; hw += mctas * kNW)
                 merge_head_parts(a.pm.lse, a.pm.part, a.sig.world, hw, D, lane, a.pm.out, a.pm.out_f16,
                                  a.pm.lse_out);
         }
