@@ -1076,7 +1076,9 @@ def split_kv_extra(args, rank, world, local):
     step a decode of each rank's page range and the merge of the ranks'
     partials, through peer memory (cottus_split_decode) and through NCCL.
     Also times each rank's decode alone, and on rank 0 the un-split decode
-    on one GPU, so the line says where the N-GPU step loses to N-fold."""
+    on one GPU, so the line says where the N-GPU step loses to N-fold; and
+    the kv-head partition of the same workload (kv_head_partition: each
+    rank decodes Hkv/N kv heads of every page, no exchange)."""
     import torch
     import torch.distributed as dist
     import cottus_b200 as cb
@@ -1098,7 +1100,11 @@ def split_kv_extra(args, rank, world, local):
         ms1 = device_ms(one, args, dev, world)
         res.update({"ms_per_step": ms1, "GB_s": w.kv_bytes() / (ms1 * 1e-3) / 1e9,
                     "frac_of_n_peaks": w.kv_bytes() / (ms1 * 1e-3) / 1e9 / peak, "ms_per_step_1gpu": ms1,
-                    "efficiency_vs_1gpu": 1.0, "gpu_launches": args.steps})
+                    "efficiency_vs_1gpu": 1.0, "gpu_launches": args.steps,
+                    "kv_head_partition": {"workload": f"all {w.Hkv} kv heads on one GPU", "exchange": "none",
+                                          "ms_per_step": ms1, "GB_s": w.kv_bytes() / (ms1 * 1e-3) / 1e9,
+                                          "frac_of_n_peaks": w.kv_bytes() / (ms1 * 1e-3) / 1e9 / peak,
+                                          "efficiency_vs_1gpu": 1.0, "gpu_launches": args.steps}})
         del t
         torch.cuda.empty_cache()
         return res
@@ -1120,18 +1126,34 @@ def split_kv_extra(args, rank, world, local):
     del t
     torch.cuda.empty_cache()
     ms1 = None
+    tf = W.device_tensors(w, dev)
     if rank == 0:
         # the same workload un-split on this GPU alone (the other ranks wait at the barrier)
-        tf = W.device_tensors(w, dev)
         one_args = argparse.Namespace(**{**vars(args)})
 
         def one(i):
             cb.paged_decode(tf["query"], tf["kv_pool"], tf["block_table"], tf["context_lens"], num_kv_heads=w.Hkv,
                             head_dim=w.D, block_size=w.bs, out=out, num_physical_blocks=w.num_blocks)
         ms1 = device_ms(one, one_args, dev, 1)
-        del tf
-        torch.cuda.empty_cache()
     dist.barrier()
+    # the kv-head partition: every rank keeps Hkv/N kv heads of every page and the query heads of their
+    # groups, and its outputs are final for those heads (no exchange, no collective in the step)
+    sh, sht = W.shard_kv_heads(w, tf, rank, world)
+    del tf
+    torch.cuda.empty_cache()
+    outh = torch.empty((w.B, sh.H, w.D), dtype=torch.float16, device=dev)
+    ms_heads = device_ms(lambda i: cb.paged_decode(sht["query"], sht["kv_pool"], sht["block_table"],
+                                                   sht["context_lens"], num_kv_heads=sh.Hkv, head_dim=w.D,
+                                                   block_size=w.bs, out=outh, num_physical_blocks=sh.num_blocks),
+                         args, dev, world)
+    del sht
+    torch.cuda.empty_cache()
+    gbh = w.kv_bytes() / (ms_heads * 1e-3) / 1e9
+    res["kv_head_partition"] = {
+        "workload": f"kv heads {sh.meta['kv_heads'][0]}.. of {w.Hkv} on rank 0: {sh.Hkv} kv / {sh.H} query heads "
+                    f"per GPU, every page", "exchange": "none", "ms_per_step": ms_heads, "GB_s": gbh,
+        "frac_of_n_peaks": gbh / (world * peak), "efficiency_vs_1gpu": (ms1 / (world * ms_heads)) if ms1 else None,
+        "gpu_launches": args.steps}
     gb = w.kv_bytes() / (ms_peer * 1e-3) / 1e9
     res.update({"exchange": "peer memory over NVLink (cottus_split_decode)", "ms_per_step": ms_peer,
                 "GB_s": gb, "frac_of_n_peaks": gb / (world * peak), "ms_per_step_nccl": ms_nccl,

@@ -39,6 +39,19 @@ def all_gather_partials(out: torch.Tensor, lse: torch.Tensor, group=None):
     return torch.stack(outs), torch.stack(lses)
 
 
+def gather_head_outputs(out: torch.Tensor, group=None) -> torch.Tensor:
+    """Outputs [B][H/world][D] of every rank's kv-head shard
+    (workloads.shard_kv_heads) gathered into [B][H][D], rank r's query heads
+    at [r*H/world, (r+1)*H/world).  The partition itself needs no exchange:
+    each rank's outputs are final for its heads; this assembles them (for a
+    caller that wants every head on every rank, and for the tests)."""
+    world = dist.get_world_size(group)
+    out = out.contiguous()
+    parts = [torch.empty_like(out) for _ in range(world)]
+    dist.all_gather(parts, out, group=group)
+    return torch.cat(parts, dim=1)
+
+
 def split_kv_decode(query, kv_pool, block_table, context_lens, *, num_kv_heads, head_dim, block_size,
                     num_layers=1, layer=0, num_physical_blocks=None, out_dtype=torch.float16, group=None,
                     part=None, lse=None, stream=None):

@@ -281,6 +281,29 @@ def shard_long_context(w: Workload, rank: int, world: int) -> Workload:
     return s
 
 
+def shard_kv_heads(w: Workload, t: dict, rank: int, world: int) -> tuple[Workload, dict]:
+    """Rank `rank` of `world` keeps kv heads [rank*Hkv/world, (rank+1)*Hkv/world)
+    of every page of the pool in t, and the query heads of their GQA groups
+    (h * Hkv / H falls in the rank's range, paged_attention_cpu.cpp:48): the
+    attention of those query heads is complete on the rank, so no partial
+    is exchanged.  Returns the shard's workload (H/world query heads,
+    Hkv/world kv heads; same block table, lengths and block ids) and its
+    device tensors: the pool [blocks][L][K|V][bs][Hkv/world][D] and the
+    query [B][H/world][D], both contiguous copies."""
+    if w.Hkv % world or w.H % w.Hkv:
+        raise ValueError("kv heads must divide evenly over the ranks, query heads over the kv heads")
+    if w.fused:
+        raise ValueError("a fused step's new k and v are not sharded by this helper")
+    hk, G = w.Hkv // world, w.H // w.Hkv
+    h0 = rank * hk
+    pool = t["kv_pool"].view(w.num_blocks, w.L, 2, w.bs, w.Hkv, w.D)[:, :, :, :, h0:h0 + hk].contiguous()
+    s = Workload(w.name, w.H // world, hk, w.D, w.bs, w.L, w.layer, w.q_dtype, w.out_dtype, w.ctx, w.block_table,
+                 w.num_blocks, w.seed, positions=w.positions, theta=w.theta)
+    s.meta = dict(w.meta, kv_heads=(h0, h0 + hk), query_heads=(h0 * G, (h0 + hk) * G))
+    ts = dict(t, kv_pool=pool.view(-1), query=t["query"][:, h0 * G:(h0 + hk) * G].contiguous())
+    return s, ts
+
+
 def host_subpool(w: Workload, kv_pool: torch.Tensor, seqs):
     """Copies the blocks used by `seqs` to the host and renumbers them densely;
     returns (pool uint16, block table int32 [len(seqs), max_blocks], ctx)."""

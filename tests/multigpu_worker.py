@@ -22,6 +22,13 @@ mode "skip":
   (the exchange is broken everywhere); after every rank recreates the
   exchange, a step is correct again.
 
+mode "heads":
+  The kv-head partition: every rank keeps Hkv/world kv heads of every page
+  and the query heads of their groups, and decodes them with
+  cottus_paged_decode; its outputs are final for those heads (no
+  exchange).  The ranks' outputs are gathered only to compare them with
+  the oracle on one sequence and with a torch fp32 attention on all.
+
 Rank 0 writes a JSON verdict."""
 import json
 import os
@@ -157,6 +164,28 @@ def skip(out_path, rank, world, dev):
             "broken_fails_fast": all(int(f[1]) for f in every), "recovered_max_abs_oracle": err, "world": world}))
 
 
+def heads(out_path, rank, world, dev):
+    import cottus_b200 as cb
+    from cottus_b200 import parallel
+    from cottus_b200 import workloads as W
+    from helpers import max_abs, oracle_outputs, torch_reference
+    from oracle.oracle import Oracle
+
+    w = W.long_ctx_70b(seed=82, B=3, context=32768)
+    t = W.device_tensors(w, dev)
+    s, st = W.shard_kv_heads(w, t, rank, world)
+    mine = cb.paged_decode(st["query"], st["kv_pool"], st["block_table"], st["context_lens"], num_kv_heads=s.Hkv,
+                           head_dim=s.D, block_size=s.bs, num_physical_blocks=s.num_blocks,
+                           out_dtype=torch.float16)
+    torch.cuda.synchronize(dev)
+    joined = parallel.gather_head_outputs(mine)
+    if rank == 0:
+        Path(out_path).write_text(json.dumps({
+            "max_abs_torch_fp32": max_abs(joined, torch_reference(w, t)),
+            "max_abs_oracle": max_abs(joined[1:2], oracle_outputs(Oracle(), w, t, [1])), "oracle_sequences": [1],
+            "heads_per_rank": s.H, "world": world}))
+
+
 def main():
     out_path, mode = sys.argv[1], sys.argv[2]
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -165,7 +194,7 @@ def main():
     torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
     try:
-        {"parity": parity, "skip": skip}[mode](out_path, rank, world, dev)
+        {"parity": parity, "skip": skip, "heads": heads}[mode](out_path, rank, world, dev)
         dist.barrier()
     finally:
         dist.destroy_process_group()

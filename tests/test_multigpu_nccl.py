@@ -6,7 +6,8 @@ every rank, over NCCL and, bit for bit the same, through peer memory
 (cottus_split_decode) over many steps with the ranks drifting up to a step
 apart.  A rank that skips a step makes the others time out, the exchange
 then refuses every step on every rank, and a recreated exchange is correct
-again."""
+again.  The kv-head partition (each rank's final outputs for its query
+heads, no exchange) matches the oracle and torch fp32 as well."""
 import json
 import os
 import socket
@@ -67,3 +68,10 @@ def test_split_kv_rank_skips_a_step(tmp_path, world):
     assert v["timed_out_untouched"] and v["broken_fails_fast"]
     assert st[3] == [0] * world
     assert v["recovered_max_abs_oracle"] <= TOL_F16
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_kv_head_partition_parity(tmp_path, world):
+    v = _run(tmp_path, world, "heads")
+    assert v["max_abs_oracle"] <= TOL_F16
+    assert v["max_abs_torch_fp32"] <= TOL_F16

@@ -1,8 +1,12 @@
-"""World-size-2 host logic of the split-KV path on CPU (gloo):
-page-range sharding of the long-context workload, the all-gather of
-(normalised partial, lse) pairs and the log-sum-exp merge, checked against
-the un-split oracle.  The partials of each shard come from the oracle, so
-this runs without a GPU; the device merge kernel is tested on the GPU."""
+"""World-size-2 host logic of the multi-GPU long-context paths on CPU
+(gloo), checked against the un-split oracle:
+  * split-KV: page-range sharding, the all-gather of (normalised partial,
+    lse) pairs and the log-sum-exp merge;
+  * kv-head partition: each rank keeps some kv heads of every page and
+    their query heads, and its outputs are final for those heads (gathered
+    here only to compare), bit for bit the oracle's.
+The per-rank results come from the oracle, so this runs without a GPU; the
+device kernels are tested on the GPU."""
 import os
 import socket
 
@@ -142,3 +146,78 @@ def test_shard_plan_covers_every_page_once():
             seen.append(s.block_table + first)
             assert int(s.ctx.sum()) == int(w.ctx.sum()) // world
         np.testing.assert_array_equal(np.concatenate(seen, axis=1), w.block_table)
+
+
+def _heads_worker(rank, world, port, result_q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    for p in (root, root / "cottus-runtime_b200", root / "tests" / "golden", root / "tests"):
+        sys.path.insert(0, str(p))
+    from helpers import oracle_outputs
+    from oracle.oracle import Oracle
+
+    from cottus_b200 import parallel
+    from cottus_b200 import workloads as W
+
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = _small_long_ctx()
+        t = W.device_tensors(w, "cpu")
+        s, ts = W.shard_kv_heads(w, t, rank, world)
+        mine = torch.from_numpy(oracle_outputs(Oracle(), s, ts, range(s.B)))
+        result_q.put((rank, parallel.gather_head_outputs(mine).numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_kv_head_partition_two_ranks_gloo():
+    from helpers import oracle_outputs
+    from oracle.oracle import Oracle
+
+    from cottus_b200 import workloads as W
+
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_heads_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r, m = q.get(timeout=240)
+        res[r] = m
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    w = _small_long_ctx()
+    full = oracle_outputs(Oracle(), w, W.device_tensors(w, "cpu"), range(w.B))
+    for r in range(world):
+        np.testing.assert_array_equal(res[r].view(np.uint32), full.view(np.uint32))
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_kv_head_shards_are_slices_of_the_pool(oracle, world):
+    """Each shard's pool holds exactly its kv heads' rows of every page, its
+    query exactly its query heads, and the oracle over the shard gives the
+    un-split oracle's rows of those heads bit for bit."""
+    from helpers import oracle_outputs
+
+    from cottus_b200 import workloads as W
+
+    w = _small_long_ctx()
+    t = W.device_tensors(w, "cpu")
+    full = oracle_outputs(oracle, w, t, range(w.B))
+    view = t["kv_pool"].view(w.num_blocks, w.L, 2, w.bs, w.Hkv, w.D)
+    for rank in range(world):
+        s, ts = W.shard_kv_heads(w, t, rank, world)
+        h0, h1 = s.meta["kv_heads"]
+        q0, q1 = s.meta["query_heads"]
+        assert (s.H, s.Hkv) == (w.H // world, w.Hkv // world)
+        assert torch.equal(ts["kv_pool"].view(w.num_blocks, w.L, 2, w.bs, s.Hkv, w.D), view[:, :, :, :, h0:h1])
+        assert torch.equal(ts["query"], t["query"][:, q0:q1])
+        got = oracle_outputs(oracle, s, ts, range(w.B))
+        np.testing.assert_array_equal(got.view(np.uint32), full[:, q0:q1].view(np.uint32))

@@ -162,9 +162,11 @@ def test_full_ragged_mha(oracle):
 
 
 def test_full_long_context_split_kv(oracle):
-    """Full 131072-token contexts: the un-split kernel, and the 2/4/8-way
-    page-range split (LSE partials on one GPU, then cottus_lse_combine),
-    against the oracle on one sequence and torch fp32 on all."""
+    """Full 131072-token contexts: the un-split kernel, the 2/4/8-way
+    page-range split (LSE partials on one GPU, then cottus_lse_combine), and
+    the 2/4/8-way kv-head partition (each shard's final outputs for its
+    query heads, the shards run one after another on one GPU), against the
+    oracle on one sequence and torch fp32 on all."""
     w = W.long_ctx_70b()
     t = W.device_tensors(w, DEV)
     out = run(w, t)
@@ -188,6 +190,15 @@ def test_full_long_context_split_kv(oracle):
         torch.cuda.synchronize()
         assert max_abs(merged, tref) <= TOL_F16
         assert max_abs(merged[5:6], ref) <= TOL_F16
+    for world in (2, 4, 8):
+        heads = []
+        for r in range(world):
+            s, st = W.shard_kv_heads(w, t, r, world)
+            heads.append(run(s, st))
+            del st
+        joined = torch.cat(heads, dim=1)
+        assert max_abs(joined, tref) <= TOL_F16
+        assert max_abs(joined[5:6], ref) <= TOL_F16
 
 
 # -- edge cases ------------------------------------------------------------------------
