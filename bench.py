@@ -742,22 +742,20 @@ def l2_plan(kv_bytes):
     L2.  KV of at least 2 x L2 per step: none needed.  Smaller KV: each step
     is one layer of a pool of L layers and the steps cycle through the
     layers, as a decode loop does, with L chosen so that a cycle covers
-    3 x L2; below 8 MB per layer that would take hundreds of layers, so the
-    step is timed alone after a 2 x L2 buffer is written instead.
-    Returns (layers, flush)."""
+    3 x L2 (hundreds of layers below 1 MB per layer: a few hundred MB of
+    HBM).  Below 8 MB per layer a step's kernel is shorter than one
+    host-side call through ctypes, so the K timed steps are captured once
+    in a CUDA graph and replayed (graph = True), as a decode engine issues
+    its per-layer launches.  Returns (layers, graph)."""
     if kv_bytes >= 2 * L2_BYTES:
         return 1, False
-    if kv_bytes >= 8 * 1024 * 1024:
-        return -(-3 * L2_BYTES // kv_bytes), False
-    return 1, True
+    return -(-3 * L2_BYTES // max(kv_bytes, 1)), kv_bytes < 8 * 1024 * 1024
 
 
-def l2_text(kv_bytes, layers, flush):
-    if flush:
-        return "L2 flushed between steps (2x L2 buffer written), each step timed alone"
+def l2_text(kv_bytes, layers, graph):
     if layers > 1:
         return (f"{layers} layers' KV cycled ({layers * kv_bytes / 1e6:.0f} MB > 126 MB L2), one layer per step, "
-                "no flush")
+                "no flush" + ("; the timed steps replayed from one CUDA graph" if graph else ""))
     return f"inputs larger than L2 ({kv_bytes / 1e6:.0f} MB KV per GPU vs 126 MB L2), no flush"
 
 
@@ -773,9 +771,9 @@ def decode_config(args, world):
     w = build_workload(args.config, 0, args.batch)
     split = args.config == "long_ctx_70b" and world > 1
     per_gpu = w.kv_bytes() // world if split else w.kv_bytes()
-    layers, flush = l2_plan(per_gpu)
+    layers, graph = l2_plan(per_gpu)
     cfg = {"workload": describe(w), "kv": "fp16", "q_out": str(w.q_dtype).replace("torch.", ""),
-           "per_gpu_batch": w.B, "kv_bytes_per_step_per_gpu": per_gpu, "l2": l2_text(per_gpu, layers, flush),
+           "per_gpu_batch": w.B, "kv_bytes_per_step_per_gpu": per_gpu, "l2": l2_text(per_gpu, layers, graph),
            "parallelism": ((f"split-KV over {world} GPUs, " +
                             ("LSE partials read from peer memory over NVLink after a completion flag raised by the "
                              "decode kernel" if args.exchange == "peer" else "NCCL all-gather of LSE partials"))
@@ -810,7 +808,7 @@ def run_decode(args, rank, world, local):
     else:
         wl = w
     kv_bytes_rank = wl.kv_bytes()
-    layers, flush = l2_plan(kv_bytes_rank)
+    layers, graph = l2_plan(kv_bytes_rank)
     if layers > 1:
         w = dataclasses.replace(w, L=layers)
         wl = w
@@ -858,29 +856,25 @@ def run_decode(args, rank, world, local):
                             head_dim=w.D, block_size=w.bs, num_layers=w.L, layer=layer, out=out,
                             num_physical_blocks=wl.num_blocks)
 
-    fbuf = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
+    # the K timed steps as one CUDA graph (short kernels: see l2_plan); captured before the warm-up
+    timed_graph = graph_of_steps(lambda i: step(args.warmup + i), args.steps, dev) if graph else None
 
     # W warm-up steps right before the K timed ones (no idle pause in between)
     sampler = start_clocks(local)
     for i in range(args.warmup):
-        if flush:
-            fbuf.fill_(float(i))
         step(i)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    if flush:
-        # L2-resident working set: flush L2 between steps, time every step alone
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
-        for i in range(args.steps):
-            fbuf.fill_(float(i))
-            evs[i][0].record(stream)
-            step(args.warmup + i)
-            evs[i][1].record(stream)
+    if graph:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        hold_gpu()
+        e0.record(stream)
+        timed_graph.replay()
+        e1.record(stream)
         torch.cuda.synchronize(dev)
-        elapsed_ms = sum(a.elapsed_time(b) for a, b in evs)
+        elapsed_ms = e0.elapsed_time(e1)
     else:
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         hold_gpu()
@@ -896,8 +890,6 @@ def run_decode(args, rank, world, local):
     # the dominant kernel alone: one decode launch between each event pair
     ka = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(50)]
     for i, (a, b) in enumerate(ka):
-        if flush:
-            fbuf.fill_(1.0)
         a.record(stream)
         if w.fused:
             step(i)
@@ -939,8 +931,8 @@ def run_decode(args, rank, world, local):
         e2e = {"value": world * kv_bytes_rank / (e_ms * 1e-3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": e_ms, "api": api,
                "pipelining": "two buffer sets; uploads and read-backs on two copy streams overlap the kernels"}
-        if flush:
-            e2e["l2"] = "steps back to back, L2 not flushed between them"
+        if graph:
+            e2e["launches"] = "direct calls through ctypes (not a graph): bound by the host-side call"
 
     if pool_snapshot is not None:
         t["kv_pool"].copy_(pool_snapshot)
@@ -958,7 +950,7 @@ def run_decode(args, rank, world, local):
 
     if exchange is not None:
         exchange.close()  # collective: every rank is done with the peer buffers
-    del t, pool_snapshot, fbuf
+    del t, pool_snapshot, timed_graph
     torch.cuda.empty_cache()
 
     extras = {}
@@ -980,7 +972,7 @@ def run_decode(args, rank, world, local):
     # launch duration for the roofline: where a step is one launch of the
     # kernel, the timed region per launch (launches back to back, as a decode
     # loop issues them); otherwise the kernel timed alone between events
-    kern_ms = ms if launches_per_step == 1 and not flush else k_ms
+    kern_ms = ms if launches_per_step == 1 else k_ms
     achieved = alg / (kern_ms * 1e-3) / 1e9
     traffic = None
     prof = ROOT / "profiles" / "traffic.json"
