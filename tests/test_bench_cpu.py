@@ -40,3 +40,19 @@ def test_reference_arm_json(config):
         import bench
         args = argparse.Namespace(config=config, batch=None, exchange="peer")
         assert d["config"] == bench.decode_config(args, 1)[1]
+
+
+def test_l2_plan_keeps_every_step_off_l2_resident_kv():
+    """Workloads smaller than 2 x L2 per step cycle enough layers' KV that a
+    cycle covers 3 x L2; below 8 MB per layer the timed steps are replayed
+    from a CUDA graph (the kernel is shorter than a host-side call)."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    l2 = bench.L2_BYTES
+    assert bench.l2_plan(2 * l2) == (1, False)
+    assert bench.l2_plan(536870912) == (1, False)  # Llama-3-8B shape, batch 64
+    for kv in (64 << 20, 8 << 20, 1380352, 4096):
+        layers, graph = bench.l2_plan(kv)
+        assert layers * kv >= 3 * l2 and (layers - 1) * kv < 3 * l2
+        assert graph == (kv < 8 << 20)
