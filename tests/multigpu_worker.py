@@ -29,7 +29,7 @@ mode "heads":
   exchange).  The ranks' outputs are gathered only to compare them with
   the oracle on one sequence and with a torch fp32 attention on all.
 
-Rank 0 writes a JSON verdict."""
+Rank 0 writes the results as JSON."""
 import json
 import os
 import random

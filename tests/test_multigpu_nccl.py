@@ -36,7 +36,7 @@ def _port():
 def _run(tmp_path, world, mode):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    out = tmp_path / f"verdict_{mode}_{world}.json"
+    out = tmp_path / f"result_{mode}_{world}.json"
     # NVLS off: a rank that leaves must not be bound to an NVLink multicast object
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
