@@ -283,19 +283,21 @@ def timed_steps(step, args, dev, world, local):
     return max_over_ranks(e0.elapsed_time(e1) / args.steps, dev, world), clocks
 
 
-def graph_of_steps(step, n, dev):
+def graph_of_steps(step, n, dev, prerun=True):
     """A CUDA graph of steps 0..n-1 (one per layer's weights): the projection
     kernels take a few microseconds, less than a host-side call through the
     ctypes layer, so the device-timed loop replays the launches as a graph,
-    as a decode engine does.  Steps run once outside the capture first (the
-    cached workspace and the kernel attributes are set up there)."""
+    as a decode engine does.  With prerun the steps run once outside the
+    capture first (the cached workspace and the kernel attributes are set up
+    there); without, the caller has run steps of the same shape already."""
     import torch
-    side = torch.cuda.Stream(dev)
-    side.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(side):
-        for i in range(n):
-            step(i)
-    torch.cuda.current_stream(dev).wait_stream(side)
+    if prerun:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            for i in range(n):
+                step(i)
+        torch.cuda.current_stream(dev).wait_stream(side)
     torch.cuda.synchronize(dev)
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
@@ -856,14 +858,14 @@ def run_decode(args, rank, world, local):
                             head_dim=w.D, block_size=w.bs, num_layers=w.L, layer=layer, out=out,
                             num_physical_blocks=wl.num_blocks)
 
-    # the K timed steps as one CUDA graph (short kernels: see l2_plan); captured before the warm-up
-    timed_graph = graph_of_steps(lambda i: step(args.warmup + i), args.steps, dev) if graph else None
-
     # W warm-up steps right before the K timed ones (no idle pause in between)
     sampler = start_clocks(local)
     for i in range(args.warmup):
         step(i)
     torch.cuda.synchronize(dev)
+    # short kernels (see l2_plan): the K timed steps captured as one CUDA graph after the warm-up, without
+    # running them first, so that the layers they read were last touched when the pool was written
+    timed_graph = graph_of_steps(lambda i: step(args.warmup + i), args.steps, dev, prerun=False) if graph else None
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
